@@ -1,0 +1,124 @@
+// Host launcher of the tcgen05 GEMM: argument validation, tile-width choice,
+// tensor maps, persistent grid sizing (one CTA per SM).
+#pragma once
+#include "gemm.cuh"
+#include "host_common.cuh"
+
+namespace vla {
+namespace gemm {
+
+// Estimated relative cost of a tile width: waves of 128 x BN tiles over the
+// SMs, each tile costing (BN + 48) column-units (48 ~ fixed A-tile and
+// epilogue overhead per tile).
+static int choose_bn(int64_t M, int64_t N, int act, int num_sms) {
+  const int cands[4] = {256, 128, 64, 32};
+  int best = 0;
+  double best_cost = 1e300;
+  for (int bn : cands) {
+    if (act == VLA_ACT_ROPE && bn % 64 != 0) continue;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + num_sms - 1) / num_sms;
+    const double cost = (double)waves * (bn + 48);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const DevEpi& ep, int64_t M, int64_t N,
+                     int64_t K, cudaStream_t st) {
+  using Cf = Cfg<BN>;
+  CUtensorMap tb;
+  int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
+  if (rc) return rc;
+  static thread_local int attr_dev_mask = 0;  // per-thread, per-device: attribute set once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cf::SMEM_BYTES));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int sms = device_info().num_sms;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  gemm_bf16_tc_kernel<BN><<<grid, kThreads, Cf::SMEM_BYTES, st>>>(ta, tb, ep, (int)M, (int)N, (int)K);
+  return launch_status("gemm_bf16_tc");
+}
+
+static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
+               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0) {
+  VLA_CHECK_ARG(A && B && C, "gemm: null operand");
+  VLA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+                (long long)K);
+  VLA_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: shape exceeds int32");
+  VLA_CHECK_ARG(N % 16 == 0, "gemm: N=%lld must be a multiple of 16", (long long)N);
+  VLA_CHECK_ARG(lda >= K && ldb >= K, "gemm: lda/ldb smaller than K");
+  VLA_CHECK_ALIGN(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0, "gemm: lda/ldb/ldc must be multiples of 8 elements");
+  VLA_CHECK_ALIGN(aligned16(A) && aligned16(B) && aligned16(C), "gemm: A/B/C must be 16-byte aligned");
+  if (M == 0) return VLA_OK;
+
+  DevEpi ep{};
+  ep.C = reinterpret_cast<bf16*>(C);
+  ep.ldc = ldc;
+  ep.alpha = 1.f;
+  ep.M = (int)M;
+  ep.N = (int)N;
+  int act = VLA_ACT_NONE;
+  if (e != nullptr) {
+    act = e->act;
+    ep.bias = reinterpret_cast<const bf16*>(e->bias);
+    ep.residual = reinterpret_cast<const bf16*>(e->residual);
+    ep.ldr = e->ldr;
+    ep.res_row_mod = e->res_row_mod;
+    ep.alpha = e->alpha == 0.f ? 1.f : e->alpha;
+    ep.rope_cs = e->rope_cs;
+    ep.rope_seq = e->rope_seq;
+    ep.rope_ncols = e->rope_ncols;
+    ep.out_grp = e->out_grp;
+    ep.out_grp_stride = e->out_grp_stride;
+    ep.euler_x = e->euler_x;
+    ep.ldx = e->ldx;
+    ep.euler_dt = e->euler_dt;
+  }
+  ep.act = act;
+  VLA_CHECK_ARG(act >= VLA_ACT_NONE && act <= VLA_ACT_EULER, "gemm: unknown act %d", act);
+  const int64_t out_cols = act == VLA_ACT_SWIGLU ? N / 2 : N;
+  VLA_CHECK_ARG(ldc >= out_cols, "gemm: ldc=%lld < output columns %lld", (long long)ldc, (long long)out_cols);
+  if (ep.residual) {
+    VLA_CHECK_ARG(ep.ldr >= out_cols, "gemm: ldr smaller than output columns");
+    VLA_CHECK_ALIGN(ep.ldr % 8 == 0 && aligned16(ep.residual), "gemm: residual must be 16-byte aligned, ldr %% 8 == 0");
+  }
+  if (ep.bias) VLA_CHECK_ALIGN(aligned16(ep.bias), "gemm: bias must be 16-byte aligned");
+  if (act == VLA_ACT_SWIGLU) {
+    VLA_CHECK_ARG(N % 32 == 0, "gemm: SwiGLU needs N %% 32 == 0");
+    VLA_CHECK_ARG(ep.bias == nullptr, "gemm: SwiGLU epilogue takes no bias");
+  }
+  if (act == VLA_ACT_ROPE) {
+    VLA_CHECK_ARG(ep.rope_cs && ep.rope_seq > 0, "gemm: RoPE needs a cos/sin table and rope_seq > 0");
+    VLA_CHECK_ARG(ep.rope_ncols % 64 == 0 && ep.rope_ncols <= N, "gemm: rope_ncols must be a multiple of 64 <= N");
+    VLA_CHECK_ARG(N % 64 == 0, "gemm: RoPE needs N %% 64 == 0");
+  }
+  if (act == VLA_ACT_EULER) {
+    VLA_CHECK_ARG(ep.euler_x != nullptr && ep.ldx >= N, "gemm: Euler needs an fp32 state with ldx >= N");
+    VLA_CHECK_ALIGN(aligned16(ep.euler_x) && ep.ldx % 4 == 0, "gemm: Euler state must be 16-byte aligned");
+  }
+
+  CUtensorMap ta;
+  int rc = make_tmap_bf16_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
+  if (rc) return rc;
+  const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
+  switch (bn) {
+    case 256: return launch_bn<256>(ta, B, ldb, ep, M, N, K, st);
+    case 128: return launch_bn<128>(ta, B, ldb, ep, M, N, K, st);
+    case 64: return launch_bn<64>(ta, B, ldb, ep, M, N, K, st);
+    case 32: return launch_bn<32>(ta, B, ldb, ep, M, N, K, st);
+    default: return set_error(VLA_E_UNSUPPORTED, "gemm: tile width %d not built", bn);
+  }
+}
+
+}  // namespace gemm
+}  // namespace vla

@@ -1,0 +1,106 @@
+// Host-side plumbing shared by every C-ABI entry point: thread-local error
+// text, argument checks, device properties, and TMA tensor-map encoding
+// through the driver entry point (no link-time dependency on libcuda).
+#pragma once
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "vla_b200.h"
+
+namespace vla {
+
+static thread_local char t_last_error[512] = "";
+
+static int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define VLA_CHECK_ARG(cond, ...) \
+  do {                           \
+    if (!(cond)) return ::vla::set_error(VLA_E_INVALID, __VA_ARGS__); \
+  } while (0)
+
+#define VLA_CHECK_ALIGN(cond, ...) \
+  do {                             \
+    if (!(cond)) return ::vla::set_error(VLA_E_ALIGN, __VA_ARGS__); \
+  } while (0)
+
+#define VLA_CUDA_TRY(expr)                                                                               \
+  do {                                                                                                   \
+    cudaError_t _e = (expr);                                                                             \
+    if (_e != cudaSuccess) return ::vla::set_error(VLA_E_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+  int num_sms = 0;
+  int max_smem_optin = 0;
+};
+
+static DeviceInfo& device_info() {
+  static DeviceInfo info[64];
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::call_once(once[dev], [dev]() {
+    cudaDeviceGetAttribute(&info[dev].num_sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&info[dev].max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (info[dev].num_sms <= 0) info[dev].num_sms = 148;
+  });
+  return info[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [outer, inner] matrix with row stride
+// ld (elements); box = [box_outer rows, box_inner cols]; 128-byte swizzle.
+// Out-of-range boxes are zero-filled by the TMA unit.
+static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                             uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tmap_encoder();
+  if (enc == nullptr) return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu box=%ux%u", (int)r,
+                     (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld, box_inner,
+                     box_outer);
+  return VLA_OK;
+}
+
+static inline cudaStream_t as_stream(vla_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static int launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(VLA_E_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return VLA_OK;
+}
+
+}  // namespace vla

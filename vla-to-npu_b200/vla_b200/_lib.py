@@ -1,0 +1,107 @@
+"""ctypes binding of libvla_b200.so (the C ABI declared in include/vla_b200.h).
+
+The library is built in-tree (``make -C vla-to-npu_b200/csrc``).  There is no
+CPU or PyTorch fallback: if the shared object is missing or a call fails, a
+``VlaError`` is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvla_b200.so")
+
+VLA_OK = 0
+VLA_E_INVALID = -1
+VLA_E_ALIGN = -2
+VLA_E_CUDA = -3
+VLA_E_UNSUPPORTED = -4
+VLA_E_DEVICE_TIMEOUT = -5
+VLA_E_WORKSPACE = -6
+
+ACT_NONE = 0
+ACT_GELU_TANH = 1
+ACT_SWIGLU = 2
+ACT_ROPE = 3
+ACT_EULER = 4
+
+
+class VlaError(RuntimeError):
+    """A libvla_b200 call returned a negative status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libvla_b200 error {code}: {msg}")
+        self.code = code
+
+
+class Epilogue(ctypes.Structure):
+    """Mirror of ``vla_epilogue`` (include/vla_b200.h)."""
+
+    _fields_ = [
+        ("bias", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("ldr", ctypes.c_int64),
+        ("res_row_mod", ctypes.c_int32),
+        ("act", ctypes.c_int32),
+        ("alpha", ctypes.c_float),
+        ("rope_seq", ctypes.c_int32),
+        ("rope_cs", ctypes.c_void_p),
+        ("rope_ncols", ctypes.c_int32),
+        ("out_grp", ctypes.c_int32),
+        ("out_grp_stride", ctypes.c_int64),
+        ("euler_x", ctypes.c_void_p),
+        ("ldx", ctypes.c_int64),
+        ("euler_dt", ctypes.c_float),
+        ("reserved", ctypes.c_int32 * 4),
+    ]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int
+_F32 = ctypes.c_float
+
+# name -> argtypes; every function returns int status unless listed in _RET.
+SIGNATURES = {
+    "vla_version": [],
+    "vla_last_error": [],
+    "vla_sync_check": [],
+    "vla_peek_device_error": [ctypes.POINTER(ctypes.c_uint)],
+    "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
+    "vla_gemm_bf16_tiled": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _P],
+}
+_RET = {"vla_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raise if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise VlaError(VLA_E_UNSUPPORTED, f"{LIB_PATH} not built (run `make -C vla-to-npu_b200/csrc`)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RET.get(name, ctypes.c_int)
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().vla_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int) -> None:
+    if rc != VLA_OK:
+        raise VlaError(rc, last_error())
+
+
+def call(name: str, *args) -> None:
+    """Invoke an entry point and raise ``VlaError`` on a negative status."""
+    check(getattr(load(), name)(*args))
