@@ -86,12 +86,16 @@ def rope_cos_sin(seq: int, head_dim: int, theta: float) -> torch.Tensor:
     return torch.cat([torch.cos(radians), torch.sin(radians)], dim=-1)
 
 
-def apply_rope(x: torch.Tensor, theta: float, positions: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Half-split rotary embedding on x [B, L, H, D] in fp32, cast back to x.dtype
-    (vla/text_encoder_bf16.py:92-104)."""
+def apply_rope(x: torch.Tensor, theta: float, positions: Optional[torch.Tensor] = None, dt=F32) -> torch.Tensor:
+    """Half-split rotary embedding on x [B, L, H, D], computed and RETURNED in fp32
+    (vla/text_encoder_bf16.py:92-104: ``x`` is rebound to its fp32 copy before
+    ``out.to(x.dtype)``, so the rotated Q/K are never rounded to bf16).  The
+    timescale is a registered buffer of the reference module, so
+    ``module.to(torch.bfloat16)`` rounds it to bf16; ``dt`` reproduces that
+    (vla/text_encoder_bf16.py:83, 95)."""
     B, L, H, D = x.shape
     d_half = D // 2
-    ts = rope_timescale(D, theta)
+    ts = rope_timescale(D, theta).to(dt).to(F32)
     if positions is None:
         positions = torch.arange(L, dtype=F32)[None, :].expand(B, -1)
     radians = positions.to(F32)[..., None] / ts[None, None, :]
@@ -102,7 +106,7 @@ def apply_rope(x: torch.Tensor, theta: float, positions: Optional[torch.Tensor] 
     out = torch.empty_like(xf)
     out[..., :d_half] = x1 * c - x2 * s
     out[..., d_half:] = x2 * c + x1 * s
-    return out.to(x.dtype)
+    return out
 
 
 def attention(q, k, v, causal: bool, kv_len: Optional[Sequence[int]] = None, dt=F32):
@@ -148,8 +152,8 @@ def text_block(x, p: Dict[str, torch.Tensor], cfg, dt=F32, kv_export: str = "rop
     q = linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D)
     k = linear(h, p["Wk"], dt=dt).view(B, L, cfg.kv_heads, D)
     v = linear(h, p["Wv"], dt=dt).view(B, L, cfg.kv_heads, D)
-    q = apply_rope(q, cfg.rope_theta)
-    k = apply_rope(k, cfg.rope_theta)
+    q = apply_rope(q, cfg.rope_theta, dt=dt)
+    k = apply_rope(k, cfg.rope_theta, dt=dt)
     ctx = attention(q, k, v, causal=True, dt=dt)
     x = linear(ctx, p["Wo"], dt=dt) + residual
     residual = x
@@ -158,7 +162,7 @@ def text_block(x, p: Dict[str, torch.Tensor], cfg, dt=F32, kv_export: str = "rop
     if kv_export == "recompute":
         hh = rms_norm(residual, p["W_norm_1"], cfg.eps, dt)
         return x, linear(hh, p["Wk"], dt=dt), linear(hh, p["Wv"], dt=dt)
-    return x, k.reshape(B, L, -1), v.reshape(B, L, -1)
+    return x, k.reshape(B, L, -1).to(dt), v.reshape(B, L, -1)
 
 
 def vision_block(x, p: Dict[str, torch.Tensor], cfg, dt=F32, gelu: str = "tanh"):
@@ -221,8 +225,8 @@ def expert_self_block(x, p, cfg, dt=F32):
     h = rms_norm(x, p["W_norm_1"], cfg.eps, dt)
     B, L, _ = h.shape
     D = cfg.head_dim
-    q = apply_rope(linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D), cfg.rope_theta)
-    k = apply_rope(linear(h, p["Wk"], dt=dt).view(B, L, cfg.kv_heads, D), cfg.rope_theta)
+    q = apply_rope(linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D), cfg.rope_theta, dt=dt)
+    k = apply_rope(linear(h, p["Wk"], dt=dt).view(B, L, cfg.kv_heads, D), cfg.rope_theta, dt=dt)
     v = linear(h, p["Wv"], dt=dt).view(B, L, cfg.kv_heads, D)
     ctx = attention(q, k, v, causal=True, dt=dt)
     x = linear(ctx, p["Wo"], dt=dt) + residual
@@ -246,7 +250,7 @@ def expert_cross_block(x, kc, vc, p, cfg, kv_len=None, dt=F32):
     B, L, _ = h.shape
     Lc = kc.shape[1]
     D = cfg.head_dim
-    q = apply_rope(linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D), cfg.rope_theta)
+    q = apply_rope(linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D), cfg.rope_theta, dt=dt)
     k = _c(kc, dt).view(B, Lc, cfg.kv_heads, D)
     v = _c(vc, dt).view(B, Lc, cfg.kv_heads, D)
     ctx = attention(q, k, v, causal=False, kv_len=kv_len, dt=dt)
