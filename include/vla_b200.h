@@ -89,6 +89,9 @@ int vla_version(void);
 int vla_sync_check(void);
 /* Device error word without clearing (0 = none). */
 int vla_peek_device_error(unsigned int* code);
+/* sizeof of the ABI structs, in the order vla_epilogue, vla_attention_args,
+ * vla_llama_layer, vla_vision_layer, written to out[0..n); returns the count. */
+int vla_abi_sizes(int64_t* out, int32_t n);
 
 /* ---------------------------------------------------------------------- */
 /* Per-op kernels (the reference's ExternalModule tops)                    */
@@ -104,6 +107,173 @@ int vla_peek_device_error(unsigned int* code);
  * 16-byte aligned.  For VLA_ACT_SWIGLU N % 32 == 0 and C has N/2 columns. */
 int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
                   int64_t K, const vla_epilogue* epi, vla_stream_t stream);
+
+/* Same GEMM with the N tile width forced (32, 64, 128 or 256) instead of chosen
+ * by the launcher's wave-count heuristic; used by tests and tile sweeps. */
+int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                        int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, vla_stream_t stream);
+
+
+/* Row normalisation over bf16 rows of width N (N % 8 == 0), fp32 statistics.
+ * RMSNorm:  y = x * rsqrt(mean(x^2) + eps) * g
+ *   replaces rms_norm_960_bf16 (cc/bf16/rms_norm_960_bf16.cc:60-62) and
+ *   rms_norm_bf16 (cc/bf16_old/rms_norm_bf16.cc:16-64) with their tiling loop
+ *   `rmsnorm` (vla/text_encoder_bf16.py:398-404).
+ * LayerNorm: y = (x - mean) * rsqrt(var + eps) * g + b
+ *   replaces layer_norm_bf16 + the bias-add region (cc/bf16_old/layer_norm_bf16.cc:16-70,
+ *   vla/vision_block_bf16.py:89-127) and `layernorm` (vla/vision_block_bf16.py:272-280).
+ * y may alias x. */
+int vla_rms_norm_bf16(const void* x, int64_t ldx, const void* g, void* y, int64_t ldy, int64_t M, int64_t N, float eps,
+                      vla_stream_t stream);
+int vla_layer_norm_bf16(const void* x, int64_t ldx, const void* g, const void* b, void* y, int64_t ldy, int64_t M,
+                        int64_t N, float eps, vla_stream_t stream);
+
+/* In-place half-split RoPE on x [M, ld]: columns [0, ncols) are 64-wide heads,
+ * row m has position m % seq; cs = fp32 [seq][64] (cos | sin) table (see
+ * vla_rope_table).  Replaces rope_apply_packed (vla/text_encoder_bf16.py:422-475)
+ * and the AIE RoPE/sin/cos kernels (cc/float/rope_vec_ops.cc:8-95,
+ * cc/float/sine.cc:117, cc/float/cosine.cc:116). */
+int vla_rope_bf16(void* x, int64_t ld, int64_t M, int32_t ncols, int32_t seq, const float* cs, vla_stream_t stream);
+
+/* Host helper: fill cs[seq][head_dim] with cos(pos / ts_k) | sin(pos / ts_k),
+ * ts_k = theta^(2k / head_dim), fp32 radians (vla/text_encoder_bf16.py:80-96). */
+int vla_rope_table(float* cs_host, int32_t seq, int32_t head_dim, double theta);
+
+/* Row softmax of x [M, N] (scores * scale), fp32 math, bf16 out.
+ * causal_row_start < 0: unmasked — softmax_bf16_32_128 (cc/bf16_old/v2_softmax_bf16.cc:627-645),
+ *   softmax_float32_seq1024 (cc/float/v1_softmax_float.cc:117-179);
+ * causal_row_start >= 0: row r masks columns > causal_row_start + r, masked
+ *   entries are written as 0 — masked_softmax_128_bf16(scores, row_start, out)
+ *   (cc/bf16/masked_softmax_128_bf16.cc:251-398). */
+int vla_softmax_bf16(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M, int64_t N, float scale,
+                     int32_t causal_row_start, vla_stream_t stream);
+
+/* Elementwise activations on [M, N] bf16, N % 8 == 0.
+ * VLA_EW_GELU_TANH : gelu_bf16 (cc/bf16_old/gelu_bf16.cc:83-102)
+ * VLA_EW_SILU      : silu_{128,160,256}_bf16 (cc/bf16/silu_160_bf16.cc:29-127)
+ * VLA_EW_SILU_MUL  : silu(x) * y2 (vla/text_encoder_bf16.py:547-581)
+ * VLA_EW_ADD       : x + y2 (cc/bf16_old/add_64_64_bf16.cc:12-49) */
+enum { VLA_EW_GELU_TANH = 0, VLA_EW_SILU = 1, VLA_EW_SILU_MUL = 2, VLA_EW_ADD = 3 };
+int vla_elementwise_bf16(int32_t op, const void* x, int64_t ldx, const void* y2, int64_t ldy2, void* out, int64_t ldo,
+                         int64_t M, int64_t N, vla_stream_t stream);
+
+/* Flash attention, head_dim 64: O = softmax(Q K^T * scale + mask) V per head.
+ * Replaces the per-head score GEMM + softmax + P.V loops of the reference
+ * blocks (vla/text_encoder_bf16.py:502-526, vla/vision_block_bf16.py:325-367,
+ * vla/action_expert_bf16.py:690-713, 765-787).  Q rows are [seq, Hq*64] per
+ * sequence (sequence b starts at q + b*q_batch), K/V [seq_k, Hkv*64]; query
+ * head h reads KV head h*Hkv/Hq.  mask: causal (key > query masked) and/or
+ * kv_len[b] (keys >= kv_len[b] masked).  Only scale == 1/8 (1/sqrt(64)) is
+ * supported. */
+typedef struct vla_attention_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t q_row, k_row, v_row, o_row;
+  int64_t q_batch, k_batch, v_batch, o_batch;
+  int32_t batch, Lq, Lk, Hq, Hkv, head_dim;
+  int32_t causal;
+  const int32_t* kv_len; /* device int32 [batch] or NULL */
+  float scale;
+} vla_attention_args;
+int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream);
+
+/* Pixel shuffle: in [B, grid*grid, C] -> out [B, (grid/s)^2, s*s*C] with
+ * out[b, (h/s)*(grid/s) + w/s, (h%s)*s*C + (w%s)*C + c] = in[b, h*grid + w, c]
+ * (con_ref, vla/vla.py:434-436; copy regions of fused_op, vla/connector_bf16.py:97-111). */
+int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, int32_t scale, int32_t C,
+                           vla_stream_t stream);
+
+/* Patch im2col for a stride == kernel conv: img [B, Cin, H, W] bf16 ->
+ * A [B*(H/p)*(W/p), Cin*p*p] (column = cin*p*p + ky*p + kx), the A operand of
+ * the patch-embedding GEMM that replaces conv_bf16 (cc/bf16_old/conv_bf16.cc:12-55)
+ * and its 14,592-call host loop (vla/preprocessing_bf16.py:86-103). */
+int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, int32_t H, int32_t W, int32_t p,
+                          vla_stream_t stream);
+
+/* Token embedding gather: out[b*rows_per_seq + row_offset + t, :] =
+ * table[ids[b*T + t], :] * scale (create_text_emb, vla/vla.py:169-174). */
+int vla_embed_bf16(const int32_t* ids, const void* table, int32_t vocab, int32_t H, int32_t B, int32_t T, float scale,
+                   void* out, int64_t ldo, int32_t rows_per_seq, int32_t row_offset, vla_stream_t stream);
+
+/* y[M, N] bf16 = x[M, N] fp32 */
+int vla_f32_to_bf16(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t M, int64_t N, vla_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Block builders                                                          */
+/* ---------------------------------------------------------------------- */
+
+/* Weights of one Llama-style layer in the library's K-major layout.
+ *   self layer : w_qkv = [Wq | Wk | Wv]^T, shape [(heads + 2 kv_heads) * 64, hidden]
+ *   cross layer: w_qkv = Wq^T, shape [heads * 64, hidden]
+ *   w_o    = Wo^T      [hidden, heads * 64]
+ *   w_gu   = gate/up interleaved: rows [32j, 32j+16) = W_gate^T rows [16j, 16j+16),
+ *            rows [32j+16, 32j+32) = W_up^T rows [16j, 16j+16); shape [2 ffn, hidden]
+ *   w_down = W_down^T  [hidden, ffn]
+ *   norm1 / norm2 = RMSNorm gains [hidden] */
+typedef struct vla_llama_layer {
+  const void* norm1;
+  const void* w_qkv;
+  const void* w_o;
+  const void* norm2;
+  const void* w_gu;
+  const void* w_down;
+  int32_t hidden, heads, kv_heads, head_dim, ffn;
+  float eps;
+} vla_llama_layer;
+
+/* Workspace bytes for vla_llama_self_layer_bf16 (qkv_out given or not) and
+ * vla_llama_cross_layer_bf16 over `rows` = batch * seq rows. */
+size_t vla_llama_layer_workspace(const vla_llama_layer* w, int64_t rows, int32_t with_qkv);
+
+/* x [batch*seq, hidden] bf16 updated in place by one causal self-attention
+ * layer: RMSNorm -> QKV GEMM with RoPE epilogue -> flash attention -> O GEMM
+ * + residual -> RMSNorm -> gate/up GEMM with SwiGLU epilogue -> down GEMM +
+ * residual.  qkv_out (optional, [rows, (heads + 2 kv_heads)*64]) receives Q,
+ * post-RoPE K and V; the K/V columns are what the action expert's cross
+ * layers attend to.
+ * Replaces text_encoder_forward (vla/text_encoder_bf16.py:480-595),
+ * llama_block_rope (vla/llama_block_rope_bf16.py:519-615) and
+ * action_expert_self_forward (vla/action_expert_bf16.py:662-728). */
+int vla_llama_self_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq, const float* rope_cs,
+                              void* qkv_out, void* workspace, size_t workspace_bytes, vla_stream_t stream);
+
+/* Cross-attention layer: Q from x (RoPE on Q only), K/V given per sequence
+ * ([kv_seq, ldkv] rows, already projected), optional key padding kv_len.
+ * Replaces action_expert_cross_forward (vla/action_expert_bf16.py:731-803)
+ * and llama_block_rope_cross (vla/llama_block_rope_bf16.py:617-709). */
+int vla_llama_cross_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq, const float* rope_cs,
+                               const void* k, const void* v, int64_t ldkv, int32_t kv_seq, const int32_t* kv_len,
+                               void* workspace, size_t workspace_bytes, vla_stream_t stream);
+
+/* SigLIP encoder layer weights (K-major): w_qkv = [Wq | Wk | Wv]^T [3 hidden, hidden],
+ * b_qkv [3 hidden], w_o [hidden, hidden], w_fc1 [ffn, hidden], w_fc2 [hidden, ffn]. */
+typedef struct vla_vision_layer {
+  const void* ln1_g;
+  const void* ln1_b;
+  const void* w_qkv;
+  const void* b_qkv;
+  const void* w_o;
+  const void* b_o;
+  const void* ln2_g;
+  const void* ln2_b;
+  const void* w_fc1;
+  const void* b_fc1;
+  const void* w_fc2;
+  const void* b_fc2;
+  int32_t hidden, heads, head_dim, ffn;
+  float eps;
+} vla_vision_layer;
+
+size_t vla_vision_layer_workspace(const vla_vision_layer* w, int64_t rows);
+
+/* x [batch*seq, hidden] updated in place: LayerNorm -> QKV GEMM + bias ->
+ * non-causal flash attention -> O GEMM + bias + residual -> LayerNorm -> fc1
+ * GEMM + bias + GELU-tanh -> fc2 GEMM + bias + residual.
+ * Replaces vision_block (vla/vision_block_bf16.py:308-420). */
+int vla_vision_layer_bf16(const vla_vision_layer* w, void* x, int32_t batch, int32_t seq, void* workspace,
+                          size_t workspace_bytes, vla_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,129 @@
+"""Block-level parity (benchmark configurations C0-C3) and the full pipeline
+(C4 structure) against the oracle: the CUDA path's error versus the fp32 oracle
+must not exceed the reference bf16 path's error (tests/parity.py)."""
+import pytest
+import torch
+
+from oracle import smolvla_ref as R
+from parity import check
+from vla_b200 import weights as W
+from vla_b200.configs import ExpertCfg, SmolVLACfg, TextCfg, VisionCfg, tiny_cfg
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+F32 = torch.float32
+
+
+def _x(shape, seed, name):
+    return W.randn(shape, seed, name, dtype=F32)
+
+
+@pytest.mark.parametrize("B,L", [(1, 128), (2, 113)])
+def test_text_block_c0(cuda, B, L):
+    from vla_b200 import device as dev
+    from vla_b200.model import LlamaLayerWeights, rope_table
+    cfg = TextCfg()
+    p = W.text_block_params(cfg, seed=0)
+    x = _x((B, L, cfg.hidden), 0, "c0.x").to(BF)
+    o32, k32, v32 = R.text_block(x, p, cfg, dt=F32)
+    obf, kbf, vbf = R.text_block(x, p, cfg, dt=BF)
+    lw = LlamaLayerWeights(p, cfg, "cuda")
+    xd = x.reshape(B * L, -1).cuda().contiguous()
+    qkv = torch.empty(B * L, cfg.q_dim + 2 * cfg.kv_dim, dtype=BF, device="cuda")
+    dev.llama_self_layer(lw.struct, xd, B, L, rope_table(L, 64, cfg.rope_theta).cuda(), dev.Workspace(), qkv_out=qkv)
+    dev.sync_check()
+    check(xd.view(B, L, -1), o32, obf, f"text block B={B} L={L} out")
+    Q, KV = cfg.q_dim, cfg.kv_dim
+    check(qkv[:, Q:Q + KV].reshape(B, L, -1), k32, kbf, "text block K (post-RoPE)")
+    check(qkv[:, Q + KV:].reshape(B, L, -1), v32, vbf, "text block V")
+
+
+def test_vision_block_c1(cuda):
+    from vla_b200 import device as dev
+    from vla_b200.model import VisionLayerWeights
+    cfg = VisionCfg()
+    p = W.vision_block_params(cfg, seed=0)
+    x = _x((1, 1024, cfg.hidden), 0, "c1.x").to(BF)
+    o32 = R.vision_block(x, p, cfg, dt=F32)
+    obf = R.vision_block(x, p, cfg, dt=BF)
+    lw = VisionLayerWeights(p, cfg, "cuda")
+    xd = x.reshape(1024, -1).cuda().contiguous()
+    dev.vision_layer(lw.struct, xd, 1, 1024, dev.Workspace())
+    dev.sync_check()
+    check(xd.view(1, 1024, -1), o32, obf, "SigLIP block C1")
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_expert_blocks_c3(cuda, B):
+    from vla_b200 import device as dev
+    from vla_b200.model import LlamaLayerWeights, rope_table
+    e, t = ExpertCfg(), TextCfg()
+    ps = W.expert_self_params(e, seed=0, layer=0)
+    pc = W.expert_cross_params(e, t.kv_dim, seed=0, layer=1)
+    x = _x((B, e.chunk, e.hidden), 0, "c3.x").to(BF)
+    tk = _x((B, 113, t.kv_dim), 0, "c3.tk").to(BF)
+    tv = _x((B, 113, t.kv_dim), 0, "c3.tv").to(BF)
+    cs = rope_table(e.chunk, 64, e.rope_theta).cuda()
+    ws = dev.Workspace()
+    # self layer
+    s32 = R.expert_self_block(x, ps, e, dt=F32)
+    sbf = R.expert_self_block(x, ps, e, dt=BF)
+    lw = LlamaLayerWeights(ps, e, "cuda")
+    xd = x.reshape(B * e.chunk, -1).cuda().contiguous()
+    dev.llama_self_layer(lw.struct, xd, B, e.chunk, cs, ws)
+    dev.sync_check()
+    check(xd.view(B, e.chunk, -1), s32, sbf, f"expert self B={B}")
+    # cross layer (K/V projections, then cross attention)
+    kc32, vc32 = R.expert_cross_kv(tk, tv, pc, dt=F32)
+    kcbf, vcbf = R.expert_cross_kv(tk, tv, pc, dt=BF)
+    c32 = R.expert_cross_block(x, kc32, vc32, pc, e, dt=F32)
+    cbf = R.expert_cross_block(x, kcbf, vcbf, pc, e, dt=BF)
+    lw = LlamaLayerWeights(pc, e, "cuda", cross=True)
+    kv = torch.empty(B * 113, 2 * e.kv_dim, dtype=BF, device="cuda")
+    dev.gemm(tk.reshape(B * 113, -1).cuda(), lw.wk_cross, kv[:, :e.kv_dim])
+    dev.gemm(tv.reshape(B * 113, -1).cuda(), lw.wv_cross, kv[:, e.kv_dim:])
+    xd = x.reshape(B * e.chunk, -1).cuda().contiguous()
+    dev.llama_cross_layer(lw.struct, xd, B, e.chunk, cs, kv[:, :e.kv_dim], kv[:, e.kv_dim:], 113, ws)
+    dev.sync_check()
+    check(xd.view(B, e.chunk, -1), c32, cbf, f"expert cross B={B}")
+
+
+def _run_model(cfg, B, seed=0):
+    from vla_b200.model import SmolVLA
+    params = W.smolvla_params(cfg, seed=seed)
+    obs = W.observation_batch(cfg, B, seed=seed + 1)
+    m = SmolVLA(cfg, params, "cuda")
+    out = m.infer(obs["images"].cuda(), obs["token_ids"].cuda(), obs["state"].cuda(), obs["noise"].cuda(),
+                  use_graph=False).clone()
+    out_graph = m.infer(obs["images"].cuda(), obs["token_ids"].cuda(), obs["state"].cuda(), obs["noise"].cuda(),
+                        use_graph=True).clone()
+    from vla_b200 import device as dev
+    dev.sync_check()
+    return params, obs, m, out, out_graph
+
+
+def test_pipeline_tiny(cuda):
+    """Whole action-chunk inference (vision, connector, prefix, text layers, 10-step
+    expert) on the scaled-down model, eager and CUDA-graph replay."""
+    cfg = tiny_cfg()
+    params, obs, m, out, out_graph = _run_model(cfg, B=3)
+    ref32 = R.smolvla_chunk(obs, params, cfg, dt=F32)
+    refbf = R.smolvla_chunk(obs, params, cfg, dt=BF)
+    check(out, ref32, refbf, "pipeline tiny (eager)")
+    assert torch.equal(out, out_graph), "graph replay differs from eager launch"
+
+
+def test_vision_tower_c2(cuda):
+    """Patch embedding + 12 SigLIP layers + post-LN + pixel shuffle + connector (C2)."""
+    from vla_b200.model import SmolVLA
+    cfg = SmolVLACfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, 1, seed=1)
+    m = SmolVLA(cfg, params, "cuda")
+    m.load_inputs(obs["images"].cuda(), obs["token_ids"].cuda(), obs["state"].cuda(), obs["noise"].cuda())
+    m.vision_tower()
+    torch.cuda.synchronize()
+    ours = m.prefix.view(1, cfg.prefix.length, -1)[:, :cfg.prefix.image_tokens]
+    ref32 = R.vision_tower(obs["images"], params, cfg, dt=F32)
+    refbf = R.vision_tower(obs["images"], params, cfg, dt=BF)
+    check(ours, ref32, refbf, "vision tower + connector C2", gate_tol=2e-1)

@@ -1,0 +1,71 @@
+"""CPU-only checks of the C ABI: the shared library loads without a GPU, it
+exports every function include/vla_b200.h declares, the ctypes struct mirrors
+match the C layouts, and host-side validation rejects bad arguments before any
+CUDA call."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from vla_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "vla_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(vla_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    unbound = [n for n in names if n not in _lib.SIGNATURES]
+    assert not unbound, f"declared but without a ctypes signature: {unbound}"
+
+
+def test_abi_struct_sizes_match_ctypes():
+    out = (ctypes.c_int64 * 4)()
+    assert _lib.load().vla_abi_sizes(out, 4) == 4
+    assert list(out) == [ctypes.sizeof(_lib.Epilogue), ctypes.sizeof(_lib.AttentionArgs),
+                         ctypes.sizeof(_lib.LlamaLayer), ctypes.sizeof(_lib.VisionLayer)]
+
+
+def test_host_validation_without_gpu():
+    lib = _lib.load()
+    # null operands are rejected before any CUDA call
+    rc = lib.vla_gemm_bf16(None, 64, None, 64, None, 64, 16, 16, 64, None, None)
+    assert rc == _lib.VLA_E_INVALID
+    assert "null" in _lib.last_error()
+    # misaligned stride
+    rc = lib.vla_gemm_bf16(ctypes.c_void_p(256), 60, ctypes.c_void_p(256), 64, ctypes.c_void_p(256), 64, 16, 16, 60,
+                           None, None)
+    assert rc == _lib.VLA_E_ALIGN
+    rc = lib.vla_llama_self_layer_bf16(None, None, 1, 1, None, None, None, 0, None)
+    assert rc == _lib.VLA_E_INVALID
+    a = _lib.AttentionArgs()
+    a.head_dim = 128
+    assert lib.vla_attention_bf16(ctypes.byref(a), None) == _lib.VLA_E_INVALID
+
+
+def test_rope_table_host_helper_matches_model_table():
+    from vla_b200.model import rope_table
+    t = torch.empty(128, 64, dtype=torch.float32)
+    _lib.call("vla_rope_table", ctypes.c_void_p(t.data_ptr()), 128, 64, 1e5)
+    torch.testing.assert_close(t, rope_table(128, 64, 1e5), atol=2e-6, rtol=1e-5)
+
+
+def test_workspace_query():
+    s = _lib.LlamaLayer()
+    s.hidden, s.heads, s.kv_heads, s.head_dim, s.ffn = 960, 15, 5, 64, 2560
+    n_with = _lib.load().vla_llama_layer_workspace(ctypes.byref(s), 113, 1)
+    n_without = _lib.load().vla_llama_layer_workspace(ctypes.byref(s), 113, 0)
+    assert n_with - n_without >= 113 * 1600 * 2
+    assert n_without >= 113 * (960 + 960 + 2560) * 2

@@ -1,0 +1,216 @@
+"""Per-op CUDA kernels vs the oracle, at the reference harness shapes
+(rms_norm/test_rms_norm_bf16.py, layer_norm/test_layer_bf16.py,
+softmax_bf16/*, vla/tests/test_masked_softmax_128_bf16.py, gelu/, silu/,
+vla/test_rope_fused.py, vla/test_pixel_shuffle.py) and the benchmark shapes."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import smolvla_ref as R
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def _rand(shape, seed, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * std).to(BF)
+
+
+@pytest.mark.parametrize("M,N", [(16, 960), (128, 960), (50, 720), (7, 768), (3, 4096), (33, 2048)])
+def test_rms_norm(cuda, M, N):
+    from vla_b200 import device as dev
+    x = _rand((M, N), M + N)
+    g = _rand((N,), 7, 0.5) + 1
+    y = dev.rms_norm(x.cuda(), g.cuda(), 1e-5)
+    ref = R.rms_norm(x, g, 1e-5, torch.float32)
+    # reference gate for the RMSNorm kernels: rtol 2e-2, atol 1e-1 (vla/tests/test_rms_norm_960_bf16.py:355)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N", [(16, 768), (1024, 768), (5, 128), (9, 3072)])
+def test_layer_norm(cuda, M, N):
+    from vla_b200 import device as dev
+    x = _rand((M, N), M * 3 + N) * 3 + 0.5
+    g = _rand((N,), 1, 0.3) + 1
+    b = _rand((N,), 2, 0.1)
+    y = dev.layer_norm(x.cuda(), g.cuda(), b.cuda(), 1e-6)
+    ref = R.layer_norm(x, g, b, 1e-6, torch.float32)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("L,heads,theta", [(128, 15, 1e5), (64, 5, 1e4), (50, 15, 1e4), (113, 20, 1e5)])
+def test_rope(cuda, L, heads, theta):
+    from vla_b200 import device as dev
+    from vla_b200.model import rope_table
+    x = _rand((L, heads * 64), L + heads)
+    cs = rope_table(L, 64, theta).cuda()
+    y = dev.rope_(x.clone().cuda(), heads * 64, L, cs)
+    ref = R.apply_rope(x.float().view(1, L, heads, 64), theta).view(L, heads * 64)
+    # reference RoPE tolerance is rtol 1e-3 / atol 1e-4 in fp32 (vla/test_rope_fused.py:153); output here is bf16
+    torch.testing.assert_close(y.float().cpu(), ref, atol=2e-2, rtol=1e-2)
+
+
+def test_rope_table_c_matches_torch(cuda):
+    import ctypes
+    from vla_b200 import _lib
+    from vla_b200.model import rope_table
+    t = torch.empty(113, 64, dtype=torch.float32)
+    _lib.call("vla_rope_table", ctypes.c_void_p(t.data_ptr()), 113, 64, 1e5)
+    torch.testing.assert_close(t, rope_table(113, 64, 1e5), atol=2e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("rows,cols,row_start", [(8, 128, 0), (8, 128, 96), (32, 128, -1), (4, 1024, -1), (32, 32, 0)])
+def test_softmax(cuda, rows, cols, row_start):
+    from vla_b200 import device as dev
+    s = _rand((rows, cols), rows + cols, 2.0)
+    y = dev.softmax(s.cuda(), 1.0, row_start).float().cpu()
+    sf = s.float()
+    if row_start >= 0:
+        mask = torch.arange(cols)[None, :] > (row_start + torch.arange(rows))[:, None]
+        sf = sf.masked_fill(mask, float("-inf"))
+    ref = torch.softmax(sf, dim=-1)
+    # masked_softmax_128 gate: rtol 5e-2, atol 5e-3 (vla/tests/test_masked_softmax_128_bf16.py:265)
+    torch.testing.assert_close(y, ref, atol=5e-3, rtol=5e-2)
+
+
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+def test_elementwise(cuda, op):
+    from vla_b200 import device as dev
+    x = _rand((64, 2560), 3, 3.0)
+    y = _rand((64, 2560), 4)
+    out = dev.elementwise(op, x.cuda(), y.cuda() if op >= 2 else None).float().cpu()
+    xf, yf = x.float(), y.float()
+    ref = [F.gelu(xf, approximate="tanh"), F.silu(xf), F.silu(xf) * yf, xf + yf][op]
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("B,grid,scale,C", [(1, 32, 4, 768), (3, 8, 4, 128), (2, 16, 2, 64)])
+def test_pixel_shuffle(cuda, B, grid, scale, C):
+    from vla_b200 import device as dev
+    x = _rand((B, grid * grid, C), B + grid)
+    out = torch.empty(B * (grid // scale) ** 2, scale * scale * C, dtype=BF, device="cuda")
+    dev.pixel_shuffle(x.reshape(-1, C).cuda(), B, grid, scale, out)
+    ref = R.pixel_shuffle(x, grid, scale).reshape(out.shape)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_im2col_matches_conv(cuda):
+    from vla_b200 import device as dev
+    img = _rand((2, 3, 64, 48), 5)
+    out = torch.empty(2 * 4 * 3, 3 * 16 * 16, dtype=BF, device="cuda")
+    dev.patch_im2col(img.cuda(), 16, out)
+    ref = F.unfold(img.float(), 16, stride=16).transpose(1, 2).reshape(out.shape)
+    assert torch.equal(out.float().cpu(), ref)
+
+
+def test_embed_gather(cuda):
+    from vla_b200 import device as dev
+    table = _rand((1000, 192), 9)
+    ids = torch.randint(0, 1000, (3, 12), generator=torch.Generator().manual_seed(1), dtype=torch.int32)
+    out = torch.zeros(3 * 17, 192, dtype=BF, device="cuda")
+    dev.embed(ids.cuda(), table.cuda(), 2.0, out, 17, 4)
+    o = out.view(3, 17, 192).cpu()
+    ref = (table.float()[ids.long()] * 2.0).to(BF)
+    assert torch.equal(o[:, 4:16], ref)
+    assert o[:, :4].abs().sum() == 0 and o[:, 16:].abs().sum() == 0
+
+
+@pytest.mark.parametrize("Lq,Lk,Hq,Hkv,causal,B", [
+    (128, 128, 15, 5, True, 1),     # C0 text self-attention
+    (113, 113, 15, 5, True, 3),     # C4 prefix (ragged tile)
+    (1024, 1024, 12, 12, False, 1),  # C1 SigLIP
+    (50, 50, 15, 5, True, 2),       # C3 expert self
+    (50, 113, 15, 5, False, 2),     # C3 expert cross
+    (1, 7, 2, 1, False, 1),
+])
+def test_attention(cuda, Lq, Lk, Hq, Hkv, causal, B):
+    from vla_b200 import device as dev
+    q = _rand((B, Lq, Hq, 64), 1)
+    k = _rand((B, Lk, Hkv, 64), 2)
+    v = _rand((B, Lk, Hkv, 64), 3)
+    o = torch.empty(B * Lq, Hq * 64, dtype=BF, device="cuda")
+    dev.attention(q.reshape(B * Lq, -1).cuda(), k.reshape(B * Lk, -1).cuda(), v.reshape(B * Lk, -1).cuda(), o,
+                  batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=Lq * Hq * 64, k_batch=Lk * Hkv * 64,
+                  v_batch=Lk * Hkv * 64, o_batch=Lq * Hq * 64, causal=causal)
+    ref = R.attention(q, k, v, causal=causal, dt=torch.float32).reshape(B * Lq, -1)
+    torch.testing.assert_close(o.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_attention_key_padding(cuda):
+    from vla_b200 import device as dev
+    B, Lq, Lk, Hq, Hkv = 3, 50, 128, 15, 5
+    q, k, v = _rand((B, Lq, Hq, 64), 4), _rand((B, Lk, Hkv, 64), 5), _rand((B, Lk, Hkv, 64), 6)
+    kv_len = torch.tensor([113, 1, 128], dtype=torch.int32)
+    o = torch.empty(B * Lq, Hq * 64, dtype=BF, device="cuda")
+    dev.attention(q.reshape(B * Lq, -1).cuda(), k.reshape(B * Lk, -1).cuda(), v.reshape(B * Lk, -1).cuda(), o,
+                  batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=Lq * Hq * 64, k_batch=Lk * Hkv * 64,
+                  v_batch=Lk * Hkv * 64, o_batch=Lq * Hq * 64, kv_len=kv_len.cuda())
+    ref = R.attention(q, k, v, causal=False, kv_len=kv_len.tolist(), dt=torch.float32).reshape(B * Lq, -1)
+    torch.testing.assert_close(o.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_gemm_epilogues(cuda):
+    """bias / GELU / residual / SwiGLU / RoPE / Euler / row-scatter epilogues vs fp32 torch."""
+    from vla_b200 import _lib, device as dev
+    from vla_b200.model import interleave_gate_up, rope_table
+    M, K = 200, 192
+    a = _rand((M, K), 11)
+    # bias + GELU + residual
+    w = _rand((256, K), 12, 0.05)
+    bias, res = _rand((256,), 13, 0.1), _rand((M, 256), 14)
+    out = torch.empty(M, 256, dtype=BF, device="cuda")
+    dev.gemm(a.cuda(), w.cuda(), out, dev.make_epilogue(bias=bias.cuda(), act=_lib.ACT_GELU_TANH,
+                                                         residual=res.cuda()))
+    ref = F.gelu(a.float() @ w.float().T + bias.float(), approximate="tanh") + res.float()
+    torch.testing.assert_close(out.float().cpu(), ref, atol=3e-2, rtol=2e-2)
+    # SwiGLU with interleaved weights
+    wg, wu = _rand((K, 320), 15, 0.05), _rand((K, 320), 16, 0.05)
+    wgu = interleave_gate_up(wg, wu, "cuda")
+    out = torch.empty(M, 320, dtype=BF, device="cuda")
+    dev.gemm(a.cuda(), wgu, out, dev.make_epilogue(act=_lib.ACT_SWIGLU))
+    ref = F.silu(a.float() @ wg.float()) * (a.float() @ wu.float())
+    torch.testing.assert_close(out.float().cpu(), ref, atol=3e-2, rtol=2e-2)
+    # RoPE on the first 2 of 3 heads, positions m % 50
+    wq = _rand((192, K), 17, 0.05)
+    cs = rope_table(50, 64, 1e4).cuda()
+    out = torch.empty(M, 192, dtype=BF, device="cuda")
+    dev.gemm(a.cuda(), wq.cuda(), out, dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=128))
+    y = (a.float() @ wq.float().T)
+    pos = torch.arange(M) % 50
+    rot = R.apply_rope(y[:, :128].reshape(M, 1, 2, 64), 1e4, positions=pos[None, :].float().t()).reshape(M, 128)
+    ref = torch.cat([rot, y[:, 128:]], dim=1)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=3e-2, rtol=2e-2)
+    # Euler: x += dt * (a @ w^T), C = bf16(x)
+    w32 = _rand((32, K), 18, 0.05)
+    x = torch.randn(M, 32, generator=torch.Generator().manual_seed(19))
+    xd = x.clone().cuda()
+    out = torch.empty(M, 32, dtype=BF, device="cuda")
+    dev.gemm(a.cuda(), w32.cuda(), out, dev.make_epilogue(act=_lib.ACT_EULER, euler_x=xd, euler_dt=-0.1))
+    ref = x - 0.1 * (a.float() @ w32.float().T)
+    torch.testing.assert_close(xd.cpu(), ref, atol=2e-3, rtol=1e-3)
+    torch.testing.assert_close(out.float().cpu(), ref, atol=2e-2, rtol=1e-2)
+    # output row scatter: rows of group g land at g*7 + r
+    out = torch.zeros(M // 4 * 7, 256, dtype=BF, device="cuda")
+    dev.gemm(a.cuda(), w.cuda(), out, dev.make_epilogue(out_grp=4, out_grp_stride=7))
+    o = out.view(M // 4, 7, 256).cpu()
+    ref = (a.float() @ w.float().T).view(M // 4, 4, 256)
+    torch.testing.assert_close(o[:, :4].float(), ref, atol=3e-2, rtol=2e-2)
+    assert o[:, 4:].abs().sum() == 0
+
+
+def test_bad_arguments_raise(cuda):
+    """Host-side validation: misaligned strides and bad shapes return errors, never launch."""
+    from vla_b200 import _lib, device as dev
+    a = torch.zeros(16, 60, dtype=BF, device="cuda")
+    w = torch.zeros(16, 60, dtype=BF, device="cuda")
+    out = torch.zeros(16, 16, dtype=BF, device="cuda")
+    with pytest.raises(_lib.VlaError) as e:
+        dev.gemm(a, w, out)  # lda 60 is not a multiple of 8
+    assert e.value.code == _lib.VLA_E_ALIGN
+    a = torch.zeros(16, 64, dtype=BF, device="cuda")
+    w = torch.zeros(20, 64, dtype=BF, device="cuda")
+    out = torch.zeros(16, 24, dtype=BF, device="cuda")
+    with pytest.raises(_lib.VlaError) as e:
+        dev.gemm(a, w, out[:, :20])  # N = 20 not a multiple of 16
+    assert e.value.code == _lib.VLA_E_INVALID

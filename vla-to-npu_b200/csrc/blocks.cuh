@@ -1,0 +1,283 @@
+// Block builders: compose the GEMM / norm / attention kernels into the
+// reference's transformer layers.  All launches go to one stream; scratch
+// lives in a caller-provided workspace (no allocation here).
+#pragma once
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemm_host.cuh"
+#include "norm.cuh"
+
+namespace vla {
+namespace blocks {
+
+static inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+static inline int grid_for(long long work, int threads) {
+  const int sms = device_info().num_sms;
+  long long blocks = (work + threads - 1) / threads;
+  const long long cap = (long long)sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const void* b, void* y, int64_t ldy, int64_t M,
+                   int64_t N, float eps, cudaStream_t st) {
+  VLA_CHECK_ARG(x && g && y && (mode == 0 || b), "norm: null pointer");
+  VLA_CHECK_ARG(M >= 0 && N > 0 && N % 8 == 0, "norm: N=%lld must be a positive multiple of 8", (long long)N);
+  VLA_CHECK_ALIGN(ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(g) && (!b || aligned16(b)),
+                  "norm: 16-byte alignment");
+  if (M == 0) return VLA_OK;
+  const int grid = (int)((M + norm::kWarps - 1) / norm::kWarps);
+  if (mode == 0)
+    norm::rownorm_kernel<0><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, nullptr,
+                                                                 (bf16*)y, ldy, (int)M, (int)N, eps);
+  else
+    norm::rownorm_kernel<1><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, (const bf16*)b,
+                                                                 (bf16*)y, ldy, (int)M, (int)N, eps);
+  return launch_status("rownorm");
+}
+
+static int attention(const attn::Params& p, int batch, cudaStream_t st) {
+  VLA_CHECK_ARG(p.q && p.k && p.v && p.o, "attention: null pointer");
+  VLA_CHECK_ARG(batch >= 0 && p.Lq >= 0 && p.Lk >= 0 && p.Hq > 0 && p.Hkv > 0 && p.Hq % p.Hkv == 0,
+                "attention: bad shape");
+  VLA_CHECK_ALIGN(aligned16(p.q) && aligned16(p.k) && aligned16(p.v) && aligned16(p.o) && p.q_row % 8 == 0 &&
+                      p.k_row % 8 == 0 && p.v_row % 8 == 0 && p.o_row % 8 == 0 && p.q_batch % 8 == 0 &&
+                      p.k_batch % 8 == 0 && p.v_batch % 8 == 0 && p.o_batch % 8 == 0,
+                  "attention: 16-byte alignment of pointers and strides");
+  if (batch == 0 || p.Lq == 0) return VLA_OK;
+  dim3 grid((p.Lq + attn::BQ - 1) / attn::BQ, p.Hq, batch);
+  attn::flash_attn_kernel<<<grid, attn::kThreads, 0, st>>>(p);
+  return launch_status("flash_attn");
+}
+
+// ----------------------------------------------------------------------------
+// Llama-style layer (text decoder block / action-expert block)
+// ----------------------------------------------------------------------------
+struct LlamaWs {
+  bf16 *h, *qkv, *attn, *mlp;
+};
+
+static size_t llama_ws_bytes(const vla_llama_layer* w, int64_t rows, bool need_qkv) {
+  const int64_t q = (int64_t)w->heads * w->head_dim, kv = (int64_t)w->kv_heads * w->head_dim;
+  size_t s = align_up(rows * w->hidden * 2) + align_up(rows * q * 2) + align_up(rows * w->ffn * 2);
+  if (need_qkv) s += align_up(rows * (q + 2 * kv) * 2);
+  return s;
+}
+
+static LlamaWs carve(const vla_llama_layer* w, int64_t rows, void* ws, bool need_qkv) {
+  const int64_t q = (int64_t)w->heads * w->head_dim;
+  uint8_t* p = (uint8_t*)ws;
+  LlamaWs r{};
+  r.h = (bf16*)p;
+  p += align_up(rows * w->hidden * 2);
+  r.attn = (bf16*)p;
+  p += align_up(rows * q * 2);
+  r.mlp = (bf16*)p;
+  p += align_up(rows * w->ffn * 2);
+  if (need_qkv) r.qkv = (bf16*)p;
+  return r;
+}
+
+static int check_llama(const vla_llama_layer* w) {
+  VLA_CHECK_ARG(w != nullptr, "llama layer: null weights");
+  VLA_CHECK_ARG(w->norm1 && w->w_qkv && w->w_o && w->norm2 && w->w_gu && w->w_down, "llama layer: null weight");
+  VLA_CHECK_ARG(w->head_dim == 64, "llama layer: head_dim must be 64");
+  VLA_CHECK_ARG(w->hidden % 16 == 0 && w->ffn % 16 == 0 && w->heads % w->kv_heads == 0,
+                "llama layer: hidden/ffn must be multiples of 16");
+  return VLA_OK;
+}
+
+// MLP half shared by self and cross layers: x += down(silu(gate(rms(x))) * up(rms(x)))
+static int llama_mlp(const vla_llama_layer* w, bf16* x, int64_t rows, const LlamaWs& ws, cudaStream_t st) {
+  const int64_t H = w->hidden, F = w->ffn;
+  int rc = rownorm(0, x, H, w->norm2, nullptr, ws.h, H, rows, H, w->eps, st);
+  if (rc) return rc;
+  vla_epilogue e{};
+  e.act = VLA_ACT_SWIGLU;
+  rc = gemm::run(ws.h, H, w->w_gu, H, ws.mlp, F, rows, 2 * F, H, &e, st);
+  if (rc) return rc;
+  vla_epilogue r{};
+  r.residual = x;
+  r.ldr = H;
+  return gemm::run(ws.mlp, F, w->w_down, F, x, H, rows, H, F, &r, st);
+}
+
+static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, const float* rope_cs, void* qkv_out,
+                      void* ws, size_t ws_bytes, cudaStream_t st) {
+  int rc = check_llama(w);
+  if (rc) return rc;
+  VLA_CHECK_ARG(xv && rope_cs && batch >= 0 && seq > 0, "llama self: bad arguments");
+  const int64_t rows = (int64_t)batch * seq;
+  const bool own_qkv = qkv_out == nullptr;
+  VLA_CHECK_ARG(ws != nullptr || rows == 0, "llama self: null workspace");
+  if (ws_bytes < llama_ws_bytes(w, rows, own_qkv))
+    return set_error(VLA_E_WORKSPACE, "llama self: workspace %zu < %zu", ws_bytes, llama_ws_bytes(w, rows, own_qkv));
+  VLA_CHECK_ALIGN(aligned16(ws) && aligned16(xv) && (own_qkv || aligned16(qkv_out)), "llama self: alignment");
+  if (rows == 0) return VLA_OK;
+  LlamaWs b = carve(w, rows, ws, own_qkv);
+  bf16* x = (bf16*)xv;
+  bf16* qkv = own_qkv ? b.qkv : (bf16*)qkv_out;
+  const int64_t H = w->hidden, Q = (int64_t)w->heads * 64, KV = (int64_t)w->kv_heads * 64, NQKV = Q + 2 * KV;
+
+  rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
+  if (rc) return rc;
+  vla_epilogue e{};
+  e.act = VLA_ACT_ROPE;
+  e.rope_cs = rope_cs;
+  e.rope_seq = seq;
+  e.rope_ncols = (int)(Q + KV);
+  rc = gemm::run(b.h, H, w->w_qkv, H, qkv, NQKV, rows, NQKV, H, &e, st);
+  if (rc) return rc;
+  attn::Params p{};
+  p.q = qkv;
+  p.k = qkv + Q;
+  p.v = qkv + Q + KV;
+  p.o = b.attn;
+  p.q_row = p.k_row = p.v_row = NQKV;
+  p.q_batch = p.k_batch = p.v_batch = (long long)seq * NQKV;
+  p.o_row = Q;
+  p.o_batch = (long long)seq * Q;
+  p.Lq = p.Lk = seq;
+  p.Hq = w->heads;
+  p.Hkv = w->kv_heads;
+  p.causal = 1;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  rc = attention(p, batch, st);
+  if (rc) return rc;
+  vla_epilogue r{};
+  r.residual = x;
+  r.ldr = H;
+  rc = gemm::run(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, st);
+  if (rc) return rc;
+  return llama_mlp(w, x, rows, b, st);
+}
+
+static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, const float* rope_cs, const void* k,
+                       const void* v, int64_t ldkv, int kv_seq, const int* kv_len, void* ws, size_t ws_bytes,
+                       cudaStream_t st) {
+  int rc = check_llama(w);
+  if (rc) return rc;
+  VLA_CHECK_ARG(xv && rope_cs && k && v && batch >= 0 && seq > 0 && kv_seq >= 0, "llama cross: bad arguments");
+  const int64_t rows = (int64_t)batch * seq;
+  const int64_t H = w->hidden, Q = (int64_t)w->heads * 64;
+  VLA_CHECK_ARG(ldkv >= (int64_t)w->kv_heads * 64, "llama cross: ldkv too small");
+  if (ws_bytes < llama_ws_bytes(w, rows, true))
+    return set_error(VLA_E_WORKSPACE, "llama cross: workspace %zu < %zu", ws_bytes, llama_ws_bytes(w, rows, true));
+  VLA_CHECK_ALIGN(aligned16(ws) && aligned16(xv), "llama cross: alignment");
+  if (rows == 0) return VLA_OK;
+  LlamaWs b = carve(w, rows, ws, true);
+  bf16* x = (bf16*)xv;
+  bf16* q = b.qkv;  // [rows, Q]
+
+  rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
+  if (rc) return rc;
+  vla_epilogue e{};
+  e.act = VLA_ACT_ROPE;
+  e.rope_cs = rope_cs;
+  e.rope_seq = seq;
+  e.rope_ncols = (int)Q;
+  rc = gemm::run(b.h, H, w->w_qkv, H, q, Q, rows, Q, H, &e, st);
+  if (rc) return rc;
+  attn::Params p{};
+  p.q = q;
+  p.k = (const bf16*)k;
+  p.v = (const bf16*)v;
+  p.o = b.attn;
+  p.q_row = Q;
+  p.q_batch = (long long)seq * Q;
+  p.k_row = p.v_row = ldkv;
+  p.k_batch = p.v_batch = (long long)kv_seq * ldkv;
+  p.o_row = Q;
+  p.o_batch = (long long)seq * Q;
+  p.Lq = seq;
+  p.Lk = kv_seq;
+  p.Hq = w->heads;
+  p.Hkv = w->kv_heads;
+  p.causal = 0;
+  p.kv_len = kv_len;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  rc = attention(p, batch, st);
+  if (rc) return rc;
+  vla_epilogue r{};
+  r.residual = x;
+  r.ldr = H;
+  rc = gemm::run(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, st);
+  if (rc) return rc;
+  return llama_mlp(w, x, rows, b, st);
+}
+
+// ----------------------------------------------------------------------------
+// SigLIP encoder layer
+// ----------------------------------------------------------------------------
+static size_t vision_ws_bytes(const vla_vision_layer* w, int64_t rows) {
+  const int64_t H = w->hidden;
+  return align_up(rows * H * 2) + align_up(rows * 3 * H * 2) + align_up(rows * H * 2) + align_up(rows * w->ffn * 2);
+}
+
+static int vision_layer(const vla_vision_layer* w, void* xv, int batch, int seq, void* ws, size_t ws_bytes,
+                        cudaStream_t st) {
+  VLA_CHECK_ARG(w && xv, "vision layer: null argument");
+  VLA_CHECK_ARG(w->ln1_g && w->ln1_b && w->w_qkv && w->b_qkv && w->w_o && w->b_o && w->ln2_g && w->ln2_b &&
+                    w->w_fc1 && w->b_fc1 && w->w_fc2 && w->b_fc2,
+                "vision layer: null weight");
+  VLA_CHECK_ARG(w->head_dim == 64 && w->heads * 64 == w->hidden, "vision layer: heads * 64 must equal hidden");
+  const int64_t rows = (int64_t)batch * seq, H = w->hidden, F = w->ffn;
+  if (ws_bytes < vision_ws_bytes(w, rows))
+    return set_error(VLA_E_WORKSPACE, "vision layer: workspace %zu < %zu", ws_bytes, vision_ws_bytes(w, rows));
+  VLA_CHECK_ALIGN(aligned16(ws) && aligned16(xv), "vision layer: alignment");
+  if (rows == 0) return VLA_OK;
+  uint8_t* p8 = (uint8_t*)ws;
+  bf16* h = (bf16*)p8;
+  p8 += align_up(rows * H * 2);
+  bf16* qkv = (bf16*)p8;
+  p8 += align_up(rows * 3 * H * 2);
+  bf16* at = (bf16*)p8;
+  p8 += align_up(rows * H * 2);
+  bf16* mlp = (bf16*)p8;
+  bf16* x = (bf16*)xv;
+
+  int rc = rownorm(1, x, H, w->ln1_g, w->ln1_b, h, H, rows, H, w->eps, st);
+  if (rc) return rc;
+  vla_epilogue e{};
+  e.bias = w->b_qkv;
+  rc = gemm::run(h, H, w->w_qkv, H, qkv, 3 * H, rows, 3 * H, H, &e, st);
+  if (rc) return rc;
+  attn::Params p{};
+  p.q = qkv;
+  p.k = qkv + H;
+  p.v = qkv + 2 * H;
+  p.o = at;
+  p.q_row = p.k_row = p.v_row = 3 * H;
+  p.q_batch = p.k_batch = p.v_batch = (long long)seq * 3 * H;
+  p.o_row = H;
+  p.o_batch = (long long)seq * H;
+  p.Lq = p.Lk = seq;
+  p.Hq = p.Hkv = w->heads;
+  p.causal = 0;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  rc = attention(p, batch, st);
+  if (rc) return rc;
+  vla_epilogue r{};
+  r.bias = w->b_o;
+  r.residual = x;
+  r.ldr = H;
+  rc = gemm::run(at, H, w->w_o, H, x, H, rows, H, H, &r, st);
+  if (rc) return rc;
+  rc = rownorm(1, x, H, w->ln2_g, w->ln2_b, h, H, rows, H, w->eps, st);
+  if (rc) return rc;
+  vla_epilogue g{};
+  g.bias = w->b_fc1;
+  g.act = VLA_ACT_GELU_TANH;
+  rc = gemm::run(h, H, w->w_fc1, H, mlp, F, rows, F, H, &g, st);
+  if (rc) return rc;
+  vla_epilogue d{};
+  d.bias = w->b_fc2;
+  d.residual = x;
+  d.ldr = H;
+  return gemm::run(mlp, F, w->w_fc2, F, x, H, rows, H, F, &d, st);
+}
+
+}  // namespace blocks
+}  // namespace vla

@@ -1,6 +1,10 @@
 // libvla_b200.so — single translation unit holding every sm_100a kernel of
 // the SmolVLA hot path and the extern "C" entry points declared in
 // include/vla_b200.h.  One TU keeps the device error word in one place.
+#include <cmath>
+#include <vector>
+
+#include "blocks.cuh"
 #include "gemm_host.cuh"
 #include "host_common.cuh"
 
@@ -29,6 +33,13 @@ int vla_peek_device_error(unsigned int* code) {
   return VLA_OK;
 }
 
+int vla_abi_sizes(int64_t* out, int32_t n) {
+  const int64_t sz[4] = {(int64_t)sizeof(vla_epilogue), (int64_t)sizeof(vla_attention_args),
+                         (int64_t)sizeof(vla_llama_layer), (int64_t)sizeof(vla_vision_layer)};
+  for (int i = 0; i < n && i < 4; ++i) out[i] = sz[i];
+  return 4;
+}
+
 int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
                   int64_t K, const vla_epilogue* epi, vla_stream_t stream) {
   return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream));
@@ -38,6 +49,162 @@ int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, 
                         int64_t N, int64_t K, const vla_epilogue* epi, int tile_n, vla_stream_t stream) {
   VLA_CHECK_ARG(tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256, "tile_n must be 32/64/128/256");
   return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n);
+}
+
+int vla_rms_norm_bf16(const void* x, int64_t ldx, const void* g, void* y, int64_t ldy, int64_t M, int64_t N, float eps,
+                      vla_stream_t stream) {
+  return blocks::rownorm(0, x, ldx, g, nullptr, y, ldy, M, N, eps, as_stream(stream));
+}
+
+int vla_layer_norm_bf16(const void* x, int64_t ldx, const void* g, const void* b, void* y, int64_t ldy, int64_t M,
+                        int64_t N, float eps, vla_stream_t stream) {
+  return blocks::rownorm(1, x, ldx, g, b, y, ldy, M, N, eps, as_stream(stream));
+}
+
+int vla_rope_bf16(void* x, int64_t ld, int64_t M, int32_t ncols, int32_t seq, const float* cs, vla_stream_t stream) {
+  VLA_CHECK_ARG(x && cs && M >= 0 && seq > 0 && ncols > 0 && ncols % 64 == 0 && ld >= ncols, "rope: bad arguments");
+  VLA_CHECK_ALIGN(aligned16(x) && ld % 8 == 0, "rope: alignment");
+  if (M == 0) return VLA_OK;
+  const long long work = M * (ncols / 64) * 4;
+  ew::rope_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((bf16*)x, ld, M, ncols, seq, cs);
+  return launch_status("rope");
+}
+
+int vla_rope_table(float* cs, int32_t seq, int32_t head_dim, double theta) {
+  VLA_CHECK_ARG(cs && seq > 0 && head_dim > 0 && head_dim % 2 == 0, "rope_table: bad arguments");
+  const int half = head_dim / 2;
+  for (int k = 0; k < half; ++k) {
+    const float expo = (2.0f / (float)head_dim) * (float)k;
+    const float ts = (float)std::pow(theta, (double)expo);
+    for (int pos = 0; pos < seq; ++pos) {
+      const float rad = (float)pos / ts;
+      cs[(size_t)pos * head_dim + k] = (float)std::cos((double)rad);
+      cs[(size_t)pos * head_dim + half + k] = (float)std::sin((double)rad);
+    }
+  }
+  return VLA_OK;
+}
+
+int vla_softmax_bf16(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M, int64_t N, float scale,
+                     int32_t causal_row_start, vla_stream_t stream) {
+  VLA_CHECK_ARG(x && y && M >= 0 && N > 0 && ldx >= N && ldy >= N, "softmax: bad arguments");
+  if (M == 0) return VLA_OK;
+  const int wpb = 8;
+  ew::softmax_kernel<<<(int)((M + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(
+      (const bf16*)x, ldx, (bf16*)y, ldy, (int)M, (int)N, scale, causal_row_start);
+  return launch_status("softmax");
+}
+
+int vla_elementwise_bf16(int32_t op, const void* x, int64_t ldx, const void* y2, int64_t ldy2, void* out, int64_t ldo,
+                         int64_t M, int64_t N, vla_stream_t stream) {
+  VLA_CHECK_ARG(op >= 0 && op <= 3, "elementwise: unknown op %d", op);
+  VLA_CHECK_ARG(x && out && (op < 2 || y2) && M >= 0 && N > 0 && N % 8 == 0, "elementwise: bad arguments");
+  VLA_CHECK_ALIGN(aligned16(x) && aligned16(out) && (op < 2 || aligned16(y2)) && ldx % 8 == 0 && ldo % 8 == 0 &&
+                      (op < 2 || ldy2 % 8 == 0),
+                  "elementwise: alignment");
+  if (M == 0) return VLA_OK;
+  ew::act_kernel<<<blocks::grid_for(M * (N / 8), 256), 256, 0, as_stream(stream)>>>(
+      (const bf16*)x, ldx, (const bf16*)y2, ldy2, (bf16*)out, ldo, M, (int)N, op);
+  return launch_status("elementwise");
+}
+
+int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream) {
+  VLA_CHECK_ARG(a != nullptr, "attention: null args");
+  VLA_CHECK_ARG(a->head_dim == 64, "attention: head_dim must be 64");
+  VLA_CHECK_ARG(std::fabs(a->scale - 0.125f) < 1e-7f, "attention: scale must be 1/sqrt(64)");
+  attn::Params p{};
+  p.q = (const bf16*)a->q;
+  p.k = (const bf16*)a->k;
+  p.v = (const bf16*)a->v;
+  p.o = (bf16*)a->o;
+  p.q_row = a->q_row;
+  p.k_row = a->k_row;
+  p.v_row = a->v_row;
+  p.o_row = a->o_row;
+  p.q_batch = a->q_batch;
+  p.k_batch = a->k_batch;
+  p.v_batch = a->v_batch;
+  p.o_batch = a->o_batch;
+  p.Lq = a->Lq;
+  p.Lk = a->Lk;
+  p.Hq = a->Hq;
+  p.Hkv = a->Hkv;
+  p.causal = a->causal;
+  p.kv_len = a->kv_len;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  return blocks::attention(p, a->batch, as_stream(stream));
+}
+
+int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, int32_t scale, int32_t C,
+                           vla_stream_t stream) {
+  VLA_CHECK_ARG(in && out && B >= 0 && grid > 0 && scale > 0 && grid % scale == 0 && C > 0 && C % 8 == 0,
+                "pixel_shuffle: bad arguments");
+  VLA_CHECK_ALIGN(aligned16(in) && aligned16(out), "pixel_shuffle: alignment");
+  if (B == 0) return VLA_OK;
+  const long long work = (long long)B * grid * grid * (C / 8);
+  ew::pixel_shuffle_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)in, (bf16*)out,
+                                                                                       B, grid, scale, C);
+  return launch_status("pixel_shuffle");
+}
+
+int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, int32_t H, int32_t W, int32_t p,
+                          vla_stream_t stream) {
+  VLA_CHECK_ARG(img && out && B >= 0 && Cin > 0 && p > 0 && H % p == 0 && W % p == 0 && p % 8 == 0,
+                "im2col: bad arguments (patch must be a multiple of 8, H and W multiples of patch)");
+  VLA_CHECK_ALIGN(aligned16(img) && aligned16(out), "im2col: alignment");
+  if (B == 0) return VLA_OK;
+  const long long work = (long long)B * (H / p) * (W / p) * (Cin * p * p / 8);
+  ew::im2col_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)img, (bf16*)out, B, Cin,
+                                                                                H, W, p);
+  return launch_status("im2col");
+}
+
+int vla_embed_bf16(const int32_t* ids, const void* table, int32_t vocab, int32_t H, int32_t B, int32_t T, float scale,
+                   void* out, int64_t ldo, int32_t rows_per_seq, int32_t row_offset, vla_stream_t stream) {
+  VLA_CHECK_ARG(ids && table && out && vocab > 0 && H > 0 && H % 8 == 0 && B >= 0 && T >= 0 && ldo >= H &&
+                    row_offset >= 0 && row_offset + T <= rows_per_seq,
+                "embed: bad arguments");
+  VLA_CHECK_ALIGN(aligned16(table) && aligned16(out) && ldo % 8 == 0, "embed: alignment");
+  if (B == 0 || T == 0) return VLA_OK;
+  const long long work = (long long)B * T * (H / 8);
+  ew::embed_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>(
+      ids, (const bf16*)table, vocab, H, B, T, scale, (bf16*)out, ldo, rows_per_seq, row_offset);
+  return launch_status("embed");
+}
+
+int vla_f32_to_bf16(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t M, int64_t N, vla_stream_t stream) {
+  VLA_CHECK_ARG(x && y && M >= 0 && N > 0 && ldx >= N && ldy >= N, "f32_to_bf16: bad arguments");
+  if (M == 0) return VLA_OK;
+  ew::f32_to_bf16_kernel<<<blocks::grid_for(M * N, 256), 256, 0, as_stream(stream)>>>(x, ldx, (bf16*)y, ldy, M,
+                                                                                      (int)N);
+  return launch_status("f32_to_bf16");
+}
+
+size_t vla_llama_layer_workspace(const vla_llama_layer* w, int64_t rows, int32_t with_qkv) {
+  if (w == nullptr || rows < 0) return 0;
+  return blocks::llama_ws_bytes(w, rows, with_qkv != 0);
+}
+
+int vla_llama_self_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq, const float* rope_cs,
+                              void* qkv_out, void* workspace, size_t workspace_bytes, vla_stream_t stream) {
+  return blocks::llama_self(w, x, batch, seq, rope_cs, qkv_out, workspace, workspace_bytes, as_stream(stream));
+}
+
+int vla_llama_cross_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq, const float* rope_cs,
+                               const void* k, const void* v, int64_t ldkv, int32_t kv_seq, const int32_t* kv_len,
+                               void* workspace, size_t workspace_bytes, vla_stream_t stream) {
+  return blocks::llama_cross(w, x, batch, seq, rope_cs, k, v, ldkv, kv_seq, kv_len, workspace, workspace_bytes,
+                             as_stream(stream));
+}
+
+size_t vla_vision_layer_workspace(const vla_vision_layer* w, int64_t rows) {
+  if (w == nullptr || rows < 0) return 0;
+  return blocks::vision_ws_bytes(w, rows);
+}
+
+int vla_vision_layer_bf16(const vla_vision_layer* w, void* x, int32_t batch, int32_t seq, void* workspace,
+                          size_t workspace_bytes, vla_stream_t stream) {
+  return blocks::vision_layer(w, x, batch, seq, workspace, workspace_bytes, as_stream(stream));
 }
 
 }  // extern "C"

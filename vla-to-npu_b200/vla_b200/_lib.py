@@ -57,6 +57,44 @@ class Epilogue(ctypes.Structure):
     ]
 
 
+class AttentionArgs(ctypes.Structure):
+    """Mirror of ``vla_attention_args``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("o", ctypes.c_void_p),
+        ("q_row", ctypes.c_int64), ("k_row", ctypes.c_int64), ("v_row", ctypes.c_int64), ("o_row", ctypes.c_int64),
+        ("q_batch", ctypes.c_int64), ("k_batch", ctypes.c_int64), ("v_batch", ctypes.c_int64),
+        ("o_batch", ctypes.c_int64),
+        ("batch", ctypes.c_int32), ("Lq", ctypes.c_int32), ("Lk", ctypes.c_int32), ("Hq", ctypes.c_int32),
+        ("Hkv", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("causal", ctypes.c_int32),
+        ("kv_len", ctypes.c_void_p), ("scale", ctypes.c_float),
+    ]
+
+
+class LlamaLayer(ctypes.Structure):
+    """Mirror of ``vla_llama_layer``."""
+
+    _fields_ = [
+        ("norm1", ctypes.c_void_p), ("w_qkv", ctypes.c_void_p), ("w_o", ctypes.c_void_p),
+        ("norm2", ctypes.c_void_p), ("w_gu", ctypes.c_void_p), ("w_down", ctypes.c_void_p),
+        ("hidden", ctypes.c_int32), ("heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("ffn", ctypes.c_int32), ("eps", ctypes.c_float),
+    ]
+
+
+class VisionLayer(ctypes.Structure):
+    """Mirror of ``vla_vision_layer``."""
+
+    _fields_ = [
+        ("ln1_g", ctypes.c_void_p), ("ln1_b", ctypes.c_void_p), ("w_qkv", ctypes.c_void_p),
+        ("b_qkv", ctypes.c_void_p), ("w_o", ctypes.c_void_p), ("b_o", ctypes.c_void_p),
+        ("ln2_g", ctypes.c_void_p), ("ln2_b", ctypes.c_void_p), ("w_fc1", ctypes.c_void_p),
+        ("b_fc1", ctypes.c_void_p), ("w_fc2", ctypes.c_void_p), ("b_fc2", ctypes.c_void_p),
+        ("hidden", ctypes.c_int32), ("heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("ffn", ctypes.c_int32), ("eps", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int
@@ -68,10 +106,34 @@ SIGNATURES = {
     "vla_last_error": [],
     "vla_sync_check": [],
     "vla_peek_device_error": [ctypes.POINTER(ctypes.c_uint)],
+    "vla_abi_sizes": [ctypes.POINTER(ctypes.c_int64), _I32],
     "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
     "vla_gemm_bf16_tiled": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _P],
+    "vla_rms_norm_bf16": [_P, _I64, _P, _P, _I64, _I64, _I64, _F32, _P],
+    "vla_layer_norm_bf16": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _F32, _P],
+    "vla_rope_bf16": [_P, _I64, _I64, _I32, _I32, _P, _P],
+    "vla_rope_table": [_P, _I32, _I32, ctypes.c_double],
+    "vla_softmax_bf16": [_P, _I64, _P, _I64, _I64, _I64, _F32, _I32, _P],
+    "vla_elementwise_bf16": [_I32, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P],
+    "vla_attention_bf16": [ctypes.POINTER(AttentionArgs), _P],
+    "vla_pixel_shuffle_bf16": [_P, _P, _I32, _I32, _I32, _I32, _P],
+    "vla_patch_im2col_bf16": [_P, _P, _I32, _I32, _I32, _I32, _I32, _P],
+    "vla_embed_bf16": [_P, _P, _I32, _I32, _I32, _I32, _F32, _P, _I64, _I32, _I32, _P],
+    "vla_f32_to_bf16": [_P, _I64, _P, _I64, _I64, _I64, _P],
+    "vla_llama_layer_workspace": [ctypes.POINTER(LlamaLayer), _I64, _I32],
+    "vla_llama_self_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, ctypes.c_size_t, _P],
+    "vla_llama_cross_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, _I64, _I32, _P, _P,
+                                   ctypes.c_size_t, _P],
+    "vla_vision_layer_workspace": [ctypes.POINTER(VisionLayer), _I64],
+    "vla_vision_layer_bf16": [ctypes.POINTER(VisionLayer), _P, _I32, _I32, _P, ctypes.c_size_t, _P],
 }
-_RET = {"vla_last_error": ctypes.c_char_p}
+_RET = {"vla_last_error": ctypes.c_char_p, "vla_llama_layer_workspace": ctypes.c_size_t,
+        "vla_vision_layer_workspace": ctypes.c_size_t}
+
+EW_GELU_TANH = 0
+EW_SILU = 1
+EW_SILU_MUL = 2
+EW_ADD = 3
 
 _lib = None
 

@@ -1,0 +1,296 @@
+"""Device-resident SmolVLA: weights uploaded once in the kernels' layout, every
+activation buffer preallocated per batch size, the whole action-chunk forward
+captured once into a CUDA graph and replayed.
+
+Pipeline (one action chunk per observation; the reference's orchestration is
+vla/vla.py:228-389 with joint_transformer vla/vla.py:194-212):
+
+  images -> im2col -> patch GEMM (+bias, +position embedding)        [B*1024, 768]
+         -> 12 SigLIP layers -> post-LayerNorm -> pixel shuffle x4   [B*64, 12288]
+         -> connector GEMM, rows scattered into the prefix           [B*113, 960]
+  ids    -> embedding gather * sqrt(960) into prefix rows 64..111
+  state  -> state GEMM into prefix row 112
+  prefix -> 16 causal text layers; odd layer i exports its post-RoPE K/V,
+            projected once per chunk by the expert's Wk_cross / Wv_cross
+  noise  -> 10 Euler steps of the 16-layer action expert (even: causal
+            self-attention over 50 tokens, odd: cross-attention to layer i's
+            prefix K/V); velocity = W_out . RMSNorm(h); the out-projection's
+            epilogue performs x += dt * v in fp32
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional
+
+import torch
+
+from . import _lib
+from . import device as dev
+from .configs import ExpertCfg, SmolVLACfg, TextCfg, VisionCfg
+
+BF16 = torch.bfloat16
+
+
+# ---------------------------------------------------------------------------
+# tables computed once on the host
+# ---------------------------------------------------------------------------
+def rope_table(seq: int, head_dim: int, theta: float) -> torch.Tensor:
+    """fp32 [seq, head_dim]: cos(pos / ts_k) | sin(pos / ts_k), ts_k = theta^(2k/D)
+    evaluated in fp32 as the reference does (vla/text_encoder_bf16.py:80-96)."""
+    ts = theta ** ((2.0 / head_dim) * torch.arange(head_dim // 2, dtype=torch.float32))
+    rad = torch.arange(seq, dtype=torch.float32)[:, None] / ts[None, :]
+    return torch.cat([torch.cos(rad), torch.sin(rad)], dim=-1).contiguous()
+
+
+def time_embedding_table(e: ExpertCfg) -> torch.Tensor:
+    """[steps, hidden] fp32: row s embeds t_s = 1 - s/steps as
+    [sin(2 pi t / p_i), cos(2 pi t / p_i)], p_i log-spaced in [min_period, max_period]."""
+    half = e.hidden // 2
+    frac = torch.linspace(0.0, 1.0, half, dtype=torch.float64)
+    period = e.min_period * (e.max_period / e.min_period) ** frac
+    rows = []
+    for s in range(e.steps):
+        t = 1.0 - s / e.steps
+        ang = 2.0 * math.pi * t / period
+        rows.append(torch.cat([torch.sin(ang), torch.cos(ang)]))
+    return torch.stack(rows).to(torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# weight layout conversion: reference [in, out] -> kernels' K-major [out, in]
+# ---------------------------------------------------------------------------
+def _kmajor(w_in_out: torch.Tensor, device) -> torch.Tensor:
+    return w_in_out.to(BF16).t().contiguous().to(device)
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, device) -> torch.Tensor:
+    """[2F, H] with rows [32j, 32j+16) = gate^T rows [16j, 16j+16) and
+    [32j+16, 32j+32) = up^T rows [16j, 16j+16) (the SwiGLU epilogue pairing)."""
+    g = w_gate.to(BF16).t().contiguous()
+    u = w_up.to(BF16).t().contiguous()
+    F_, H = g.shape
+    assert F_ % 16 == 0
+    out = torch.stack([g.view(F_ // 16, 16, H), u.view(F_ // 16, 16, H)], dim=1).reshape(2 * F_, H)
+    return out.contiguous().to(device)
+
+
+class LlamaLayerWeights:
+    """One text-decoder or action-expert layer on the device."""
+
+    def __init__(self, p: Dict[str, torch.Tensor], cfg, device, cross: bool = False):
+        self.cross = cross
+        if cross:
+            self.w_qkv = _kmajor(p["Wq"], device)
+            self.wk_cross = _kmajor(p["Wk_cross"], device)
+            self.wv_cross = _kmajor(p["Wv_cross"], device)
+        else:
+            self.w_qkv = _kmajor(torch.cat([p["Wq"], p["Wk"], p["Wv"]], dim=1), device)
+        self.w_o = _kmajor(p["Wo"], device)
+        self.w_gu = interleave_gate_up(p["W_gate"], p["W_up"], device)
+        self.w_down = _kmajor(p["W_down"], device)
+        self.norm1 = p["W_norm_1"].to(BF16).contiguous().to(device)
+        self.norm2 = p["W_norm_2"].to(BF16).contiguous().to(device)
+        s = _lib.LlamaLayer()
+        s.norm1, s.w_qkv, s.w_o = self.norm1.data_ptr(), self.w_qkv.data_ptr(), self.w_o.data_ptr()
+        s.norm2, s.w_gu, s.w_down = self.norm2.data_ptr(), self.w_gu.data_ptr(), self.w_down.data_ptr()
+        s.hidden, s.heads, s.kv_heads, s.head_dim, s.ffn = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn
+        s.eps = cfg.eps
+        self.struct = s
+
+
+class VisionLayerWeights:
+    def __init__(self, p: Dict[str, torch.Tensor], cfg: VisionCfg, device):
+        H = cfg.hidden
+        z = torch.zeros(H, dtype=BF16)
+        self.w_qkv = _kmajor(torch.cat([p["Wq"], p["Wk"], p["Wv"]], dim=1), device)
+        self.b_qkv = torch.cat([p.get("bq", z), p.get("bk", z), p.get("bv", z)]).to(BF16).contiguous().to(device)
+        self.w_o = _kmajor(p["Wo"], device)
+        self.b_o = p.get("bo", z).to(BF16).contiguous().to(device)
+        self.w_fc1 = _kmajor(p["W_up"], device)
+        self.b_fc1 = p.get("b_up", torch.zeros(cfg.ffn, dtype=BF16)).to(BF16).contiguous().to(device)
+        self.w_fc2 = _kmajor(p["W_down"], device)
+        self.b_fc2 = p.get("b_down", z).to(BF16).contiguous().to(device)
+        self.ln = [p[k].to(BF16).contiguous().to(device) for k in ("W_norm_1", "b_norm_1", "W_norm_2", "b_norm_2")]
+        s = _lib.VisionLayer()
+        s.ln1_g, s.ln1_b, s.ln2_g, s.ln2_b = (t.data_ptr() for t in self.ln)
+        s.w_qkv, s.b_qkv, s.w_o, s.b_o = (self.w_qkv.data_ptr(), self.b_qkv.data_ptr(), self.w_o.data_ptr(),
+                                          self.b_o.data_ptr())
+        s.w_fc1, s.b_fc1, s.w_fc2, s.b_fc2 = (self.w_fc1.data_ptr(), self.b_fc1.data_ptr(), self.w_fc2.data_ptr(),
+                                              self.b_fc2.data_ptr())
+        s.hidden, s.heads, s.head_dim, s.ffn, s.eps = H, cfg.heads, cfg.head_dim, cfg.ffn, cfg.eps
+        self.struct = s
+
+
+# ---------------------------------------------------------------------------
+# the model
+# ---------------------------------------------------------------------------
+class SmolVLA:
+    """SmolVLA action-chunk inference on one GPU (observations along the batch)."""
+
+    def __init__(self, cfg: SmolVLACfg, params: dict, device="cuda"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        d = self.device
+        v, t, e, pf = cfg.vision, cfg.text, cfg.expert, cfg.prefix
+        assert v.tokens // cfg.connector.scale ** 2 == pf.image_tokens, "pixel shuffle must yield the image tokens"
+        pp = params["patch"]
+        self.w_patch = pp["kernel"].to(BF16).reshape(v.hidden, -1).contiguous().to(d)  # [hidden, 3*p*p], K-major
+        self.b_patch = pp["b_patch"].to(BF16).contiguous().to(d)
+        self.pos_emb = pp["pos_emb"].to(BF16).contiguous().to(d)
+        self.post_g = pp["W_post_norm"].to(BF16).contiguous().to(d)
+        self.post_b = pp["b_post_norm"].to(BF16).contiguous().to(d)
+        self.vision = [VisionLayerWeights(p, v, d) for p in params["vision"]]
+        self.w_conn = _kmajor(params["connector"]["W"], d)
+        self.embed_table = params["embed"].to(BF16).contiguous().to(d)
+        self.w_state = _kmajor(params["W_state"], d)
+        self.text = [LlamaLayerWeights(p, t, d) for p in params["text"]]
+        self.expert = [LlamaLayerWeights(p, e, d, cross=(i % 2 == 1)) for i, p in enumerate(params["expert"])]
+        self.w_in = _kmajor(params["W_action_in"], d)
+        self.exp_norm = params["W_exp_norm"].to(BF16).contiguous().to(d)
+        self.w_out = _kmajor(params["W_action_out"], d)
+        self.temb = time_embedding_table(e).to(BF16).to(d)
+        self.rope_text = rope_table(pf.length, t.head_dim, t.rope_theta).to(d)
+        self.rope_exp = rope_table(e.chunk, e.head_dim, e.rope_theta).to(d)
+        self.ws = dev.Workspace(d)
+        self.batch = 0
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.graph_batch = 0
+
+    # -- buffers ----------------------------------------------------------
+    def allocate(self, batch: int) -> None:
+        if batch == self.batch:
+            return
+        cfg, d = self.cfg, self.device
+        v, t, e, pf = cfg.vision, cfg.text, cfg.expert, cfg.prefix
+        self.batch = batch
+        B = batch
+        self.in_images = torch.empty(B, v.channels, v.image, v.image, dtype=BF16, device=d)
+        self.in_ids = torch.empty(B, pf.text_tokens, dtype=torch.int32, device=d)
+        self.in_state = torch.empty(B, pf.state_dim, dtype=BF16, device=d)
+        self.in_noise = torch.empty(B * e.chunk, e.action_dim, dtype=torch.float32, device=d)
+        rows_v = B * v.tokens
+        k2 = v.hidden * cfg.connector.scale ** 2
+        self.patches = torch.empty(rows_v, v.patch_dim, dtype=BF16, device=d)
+        self.x_vis = torch.empty(rows_v, v.hidden, dtype=BF16, device=d)
+        self.x_ln = torch.empty(rows_v, v.hidden, dtype=BF16, device=d)
+        self.shuffled = torch.empty(B * pf.image_tokens, k2, dtype=BF16, device=d)
+        rows_t = B * pf.length
+        self.prefix = torch.empty(rows_t, t.hidden, dtype=BF16, device=d)
+        self.qkv = torch.empty(rows_t, t.q_dim + 2 * t.kv_dim, dtype=BF16, device=d)
+        n_cross = sum(1 for w in self.expert if w.cross)
+        self.kv_cross = torch.empty(n_cross, rows_t, 2 * e.kv_dim, dtype=BF16, device=d)
+        rows_e = B * e.chunk
+        self.x_t = torch.empty(rows_e, e.action_dim, dtype=torch.float32, device=d)
+        self.x_b = torch.empty(rows_e, e.action_dim, dtype=BF16, device=d)
+        self.h = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
+        self.hn = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
+        lib = _lib.load()
+        import ctypes
+        need = max(
+            lib.vla_vision_layer_workspace(ctypes.byref(self.vision[0].struct), rows_v) if self.vision else 0,
+            lib.vla_llama_layer_workspace(ctypes.byref(self.text[0].struct), rows_t, 0),
+            max(lib.vla_llama_layer_workspace(ctypes.byref(w.struct), rows_e, 1) for w in self.expert),
+        )
+        self.ws.get(need)
+        self.graph = None
+
+    # -- stages -----------------------------------------------------------
+    def vision_tower(self) -> None:
+        cfg = self.cfg
+        v, t, pf = cfg.vision, cfg.text, cfg.prefix
+        B = self.batch
+        dev.patch_im2col(self.in_images, v.patch, self.patches)
+        dev.gemm(self.patches, self.w_patch, self.x_vis,
+                 dev.make_epilogue(bias=self.b_patch, residual=self.pos_emb, res_row_mod=v.tokens))
+        for lw in self.vision:
+            dev.vision_layer(lw.struct, self.x_vis, B, v.tokens, self.ws)
+        dev.layer_norm(self.x_vis, self.post_g, self.post_b, v.eps, out=self.x_ln)
+        dev.pixel_shuffle(self.x_ln, B, v.grid, cfg.connector.scale, self.shuffled)
+        # connector rows of observation b land in prefix rows [b*113, b*113 + 64)
+        dev.gemm(self.shuffled, self.w_conn, self.prefix,
+                 dev.make_epilogue(out_grp=pf.image_tokens, out_grp_stride=pf.length))
+
+    def prefix_tokens(self) -> None:
+        t, pf = self.cfg.text, self.cfg.prefix
+        scale = math.sqrt(t.hidden) if pf.embed_scale_sqrt_hidden else 1.0
+        dev.embed(self.in_ids, self.embed_table, scale, self.prefix, pf.length, pf.image_tokens)
+        # state projection -> row 112 of each observation (row stride = prefix length)
+        state_rows = self.prefix[pf.image_tokens + pf.text_tokens:].as_strided(
+            (self.batch, t.hidden), (pf.length * t.hidden, 1))
+        dev.gemm(self.in_state, self.w_state, state_rows)
+
+    def text_layers(self) -> None:
+        t, pf, e = self.cfg.text, self.cfg.prefix, self.cfg.expert
+        Q, KV = t.q_dim, t.kv_dim
+        ci = 0
+        for i, lw in enumerate(self.text):
+            dev.llama_self_layer(lw.struct, self.prefix, self.batch, pf.length, self.rope_text, self.ws,
+                                 qkv_out=self.qkv)
+            if i < len(self.expert) and self.expert[i].cross:
+                ew = self.expert[i]
+                kvc = self.kv_cross[ci]
+                dev.gemm(self.qkv[:, Q:Q + KV], ew.wk_cross, kvc[:, :e.kv_dim])
+                dev.gemm(self.qkv[:, Q + KV:Q + 2 * KV], ew.wv_cross, kvc[:, e.kv_dim:])
+                ci += 1
+
+    def action_expert(self) -> None:
+        e, pf = self.cfg.expert, self.cfg.prefix
+        B = self.batch
+        self.x_t.copy_(self.in_noise)
+        dev.f32_to_bf16(self.x_t, self.x_b)
+        dt = -1.0 / e.steps
+        for s in range(e.steps):
+            dev.gemm(self.x_b, self.w_in, self.h, dev.make_epilogue(bias=self.temb[s]))
+            ci = 0
+            for lw in self.expert:
+                if lw.cross:
+                    kvc = self.kv_cross[ci]
+                    dev.llama_cross_layer(lw.struct, self.h, B, e.chunk, self.rope_exp, kvc[:, :e.kv_dim],
+                                          kvc[:, e.kv_dim:], pf.length, self.ws)
+                    ci += 1
+                else:
+                    dev.llama_self_layer(lw.struct, self.h, B, e.chunk, self.rope_exp, self.ws)
+            dev.rms_norm(self.h, self.exp_norm, e.eps, out=self.hn)
+            dev.gemm(self.hn, self.w_out, self.x_b,
+                     dev.make_epilogue(act=_lib.ACT_EULER, euler_x=self.x_t, euler_dt=dt))
+
+    def forward_device(self) -> torch.Tensor:
+        """Launch the whole chunk forward on the current stream from the input buffers."""
+        self.vision_tower()
+        self.prefix_tokens()
+        self.text_layers()
+        self.action_expert()
+        return self.x_t
+
+    # -- graph ------------------------------------------------------------
+    def capture(self) -> None:
+        self.forward_device()  # warm-up: sets kernel attributes, touches every buffer
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.forward_device()
+        torch.cuda.synchronize(self.device)
+        self.graph = g
+        self.graph_batch = self.batch
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None or self.graph_batch != self.batch:
+            self.capture()
+        self.graph.replay()
+        return self.x_t
+
+    # -- public API -------------------------------------------------------
+    def load_inputs(self, images, token_ids, state, noise, non_blocking: bool = True) -> None:
+        """Copy one batch of observations (host or device tensors) into the input buffers."""
+        B = images.shape[0]
+        self.allocate(B)
+        self.in_images.copy_(images.to(BF16) if images.dtype != BF16 else images, non_blocking=non_blocking)
+        self.in_ids.copy_(token_ids, non_blocking=non_blocking)
+        self.in_state.copy_(state.to(BF16) if state.dtype != BF16 else state, non_blocking=non_blocking)
+        self.in_noise.copy_(noise.reshape(B * self.cfg.expert.chunk, -1), non_blocking=non_blocking)
+
+    def infer(self, images, token_ids, state, noise, use_graph: bool = True) -> torch.Tensor:
+        """Action chunks [B, chunk, action_dim] (fp32) for a batch of observations."""
+        self.load_inputs(images, token_ids, state, noise)
+        out = self.replay() if use_graph else self.forward_device()
+        return out.view(self.batch, self.cfg.expert.chunk, self.cfg.expert.action_dim)
