@@ -1,0 +1,540 @@
+#!/usr/bin/env python
+"""SmolVLA action-chunk inference benchmark on 1..8 B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Workload (benchmark configuration C4, end-to-end): per observation one 512x512
+image through the 12-layer SigLIP tower and the pixel-shuffle connector, 48
+text tokens + 1 state token, a 113-token prefix through 16 text layers, then
+the 16-layer action expert for 10 Euler steps -> one 50x32 action chunk.  One
+step = one batch of B observations per GPU (default 256, the largest C4 batch);
+observations are partitioned across ranks with no collective on the data path
+(weak scaling: every rank runs B).  Weights are random and seeded, inputs are
+synthetic with the benchmark's distributions.
+
+The default arm times the CUDA path: the whole chunk forward is one CUDA graph
+replay, timed with CUDA events between a barrier + synchronize on both sides,
+max over ranks.  ``e2e`` times the public host API (host->device copies of
+the observations and device->host copy of the actions inside the timed
+region).  ``roofline`` comes from an eager pass with the library's launch
+profiler.  ``cpu_baseline`` and ``--impl reference`` time the reference's own
+CPU path (the oracle's bf16 restatement of its torch modules) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vla-to-npu_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "SmolVLA action chunks/sec"
+UNIT = "chunks/s"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=256, help="observations per GPU per step")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip block timings, batch sweep and CPU baseline")
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--kernel-case", default="",
+                    help="run one kernel of the step on a fixed small case (for ncu captures) and print its timing: "
+                         + ", ".join(KERNEL_CASES))
+    return ap.parse_args()
+
+
+# name -> description; shapes are one GPU's share of the C4 step at 16 observations
+# (inputs larger than L2, a few hundred MB on the device)
+KERNEL_CASES = {
+    "gemm_fc1": "SigLIP fc1 GEMM + bias + GELU, M=16384 N=3072 K=768",
+    "gemm_qkv": "SigLIP QKV GEMM + bias, M=16384 N=2304 K=768",
+    "gemm_fc2": "SigLIP fc2 GEMM + bias + residual, M=16384 N=768 K=3072",
+    "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
+    "layer_norm": "SigLIP LayerNorm, 16384 x 768",
+}
+
+
+def run_kernel_case(args):
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    from vla_b200 import weights as W
+    torch.cuda.set_device(0)
+    name = args.kernel_case
+    if name not in KERNEL_CASES:
+        raise SystemExit(f"unknown kernel case {name!r}; choose from {list(KERNEL_CASES)}")
+    bf = torch.bfloat16
+    if name.startswith("gemm"):
+        M, N, K = {"gemm_fc1": (16384, 3072, 768), "gemm_qkv": (16384, 2304, 768),
+                   "gemm_fc2": (16384, 768, 3072)}[name]
+        a = W.randn((M, K), 0, "kc.a").cuda()
+        w = W.randn((N, K), 0, "kc.w", std=0.02).cuda()
+        b = W.randn((N,), 0, "kc.b", std=0.01).cuda()
+        c = torch.empty(M, N, dtype=bf, device="cuda")
+        res = W.randn((M, N), 0, "kc.r").cuda() if name == "gemm_fc2" else None
+        epi = dev.make_epilogue(bias=b, residual=res, act=_lib.ACT_GELU_TANH if name == "gemm_fc1" else 0)
+        fn = lambda: dev.gemm(a, w, c, epi)  # noqa: E731
+        flops, nbytes = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * N * (2 if res is not None else 1))
+    elif name == "attn_vision":
+        B, L, H = 16, 1024, 12
+        qkv = W.randn((B * L, 3 * H * 64), 0, "kc.qkv").cuda()
+        o = torch.empty(B * L, H * 64, dtype=bf, device="cuda")
+        fn = lambda: dev.attention(qkv[:, :H * 64], qkv[:, H * 64:2 * H * 64], qkv[:, 2 * H * 64:], o,  # noqa: E731
+                                   batch=B, Lq=L, Lk=L, Hq=H, Hkv=H, q_batch=L * 3 * H * 64, k_batch=L * 3 * H * 64,
+                                   v_batch=L * 3 * H * 64, o_batch=L * H * 64)
+        flops, nbytes = 4.0 * B * H * L * L * 64, 2.0 * B * L * H * 64 * 4
+    else:
+        x = W.randn((16384, 768), 0, "kc.x").cuda()
+        g, bb = torch.ones(768, dtype=bf, device="cuda"), torch.zeros(768, dtype=bf, device="cuda")
+        y = torch.empty_like(x)
+        fn = lambda: dev.layer_norm(x, g, bb, 1e-6, out=y)  # noqa: E731
+        flops, nbytes = 0.0, 4.0 * 16384 * 768
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    dev.sync_check()
+    print(json.dumps({"kernel_case": name, "what": KERNEL_CASES[name], "ms": ms,
+                      "tflops": flops / ms / 1e9 if flops else None, "gbs": nbytes / ms / 1e6}), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(backend="nccl"):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 10:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        power = [num(r[3]) for r in rows if num(r[3]) is not None]
+        loaded = [num(r[1]) for r in rows if num(r[3]) is not None and num(r[3]) > 300 and num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(loaded or sm) if (loaded or sm) else None,
+                "sm_max_mhz": num(rows[0][2]), "reasons": reasons, "samples": len(rows),
+                "samples_under_load": len(loaded), "power_w_max": max(power) if power else None,
+                "mem_mhz": statistics.median([num(r[9]) for r in rows if num(r[9]) is not None] or [0])}
+
+
+# ---------------------------------------------------------------------------
+# the CPU path (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+def cpu_chunk_seconds(n_obs: int, threads: int) -> tuple:
+    """Time the reference's own bf16 CPU path (oracle restatement of its torch modules)
+    for ``n_obs`` full action chunks (one observation each); returns (seconds, threads)."""
+    from oracle import smolvla_ref as R
+    from vla_b200 import weights as W
+    from vla_b200.configs import SmolVLACfg
+    if threads > 0:
+        torch.set_num_threads(threads)
+    cfg = SmolVLACfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, 1, seed=1)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        for _ in range(n_obs):
+            R.smolvla_chunk(obs, params, cfg, dt=torch.bfloat16)
+        dt = time.perf_counter() - t0
+    return dt, torch.get_num_threads()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = args.cpu_threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    from oracle import smolvla_ref as R
+    from vla_b200 import weights as W
+    from vla_b200.configs import SmolVLACfg
+    cfg = SmolVLACfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, 1, seed=1)
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            R.smolvla_chunk(obs, params, cfg, dt=torch.bfloat16)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            R.smolvla_chunk(obs, params, cfg, dt=torch.bfloat16)
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = 1.0 / sec
+    sample = ("1 observation per step (one full action chunk: vision tower, prefix, 16 text layers, "
+              "10 Euler steps of the 16-layer expert) through the bf16 CPU restatement of the reference's "
+              "torch modules")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights and observations)",
+        "config": workload_config(args, 1, 1),
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, batch, world):
+    return {
+        "workload": "C4 end-to-end SmolVLA action-chunk inference: 512x512 image -> 12 SigLIP layers -> "
+                    "pixel-shuffle connector; 113-token prefix -> 16 text layers; 16-layer action expert x 10 "
+                    "Euler steps -> 50x32 action chunk",
+        "global_batch": batch * world, "per_gpu_batch": batch, "prefix_tokens": 113, "image": 512,
+        "vision_layers": 12, "text_layers": 16, "expert_layers": 16, "euler_steps": 10, "chunk": 50,
+        "parallelism": f"dp{world} (observations partitioned, no collective on the data path)",
+        "l2_policy": "working set larger than L2 (0.8 GB of weights + per-step activations), no flush",
+    }
+
+
+# ---------------------------------------------------------------------------
+# the CUDA path
+# ---------------------------------------------------------------------------
+def profile_pass(model) -> dict:
+    """Eager forward under the launch profiler; the queue is pre-filled behind a
+    sleep kernel so launch gaps do not enter the per-kernel device times."""
+    from vla_b200 import _lib
+    import ctypes
+    lib = _lib.load()
+    cap = 8192
+    _lib.call("vla_profile_start", cap)
+    torch.cuda._sleep(400_000_000)
+    model.forward_device()
+    recs = (_lib.ProfileRecord * cap)()
+    n = ctypes.c_int32(0)
+    _lib.call("vla_profile_stop", recs, cap, ctypes.byref(n))
+    agg = {}
+    for i in range(min(n.value, cap)):
+        r = recs[i]
+        k = _lib.KIND_NAMES[r.kind]
+        a = agg.setdefault(k, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+        a["launches"] += 1
+        a["ms"] += r.ms
+        a["flops"] += r.flops
+        a["bytes"] += r.bytes
+    del lib
+    return agg
+
+
+def block_timings(torch_mod, reps=20) -> dict:
+    """Per-block device time (us) at the C0-C3 configurations, B=1, via graph replay."""
+    from vla_b200 import device as dev
+    from vla_b200 import weights as W
+    from vla_b200.configs import ExpertCfg, TextCfg, VisionCfg
+    from vla_b200.model import LlamaLayerWeights, VisionLayerWeights, rope_table
+    out = {}
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps * 1e3
+
+    ws = dev.Workspace()
+    t = TextCfg()
+    lw = LlamaLayerWeights(W.text_block_params(t), t, "cuda")
+    x = W.randn((128, t.hidden), 0, "b.x").cuda()
+    cs = rope_table(128, 64, t.rope_theta).cuda()
+    qkv = torch.empty(128, t.q_dim + 2 * t.kv_dim, dtype=torch.bfloat16, device="cuda")
+    dev.llama_self_layer(lw.struct, x, 1, 128, cs, ws, qkv_out=qkv)
+    out["C0_text_block_us"] = timed(lambda: dev.llama_self_layer(lw.struct, x, 1, 128, cs, ws, qkv_out=qkv))
+    v = VisionCfg()
+    vw = VisionLayerWeights(W.vision_block_params(v), v, "cuda")
+    xv = W.randn((1024, v.hidden), 0, "b.xv").cuda()
+    dev.vision_layer(vw.struct, xv, 1, 1024, ws)
+    out["C1_siglip_block_us"] = timed(lambda: dev.vision_layer(vw.struct, xv, 1, 1024, ws))
+    return out
+
+
+def run_ours(args, rank, world, local):
+    from vla_b200 import _lib
+    from vla_b200 import weights as W
+    from vla_b200.configs import SmolVLACfg
+    from vla_b200.model import SmolVLA
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = SmolVLACfg()
+    B = args.batch
+    params = W.smolvla_params(cfg, seed=0)
+    model = SmolVLA(cfg, params, dev)
+    del params
+    obs = W.observation_batch(cfg, B, seed=1 + rank)
+    host = {
+        "images": obs["images"].pin_memory(),
+        "token_ids": obs["token_ids"].pin_memory(),
+        "state": obs["state"].pin_memory(),
+        "noise": obs["noise"].pin_memory(),
+    }
+    dev_in = {k: v.to(dev) for k, v in host.items()}
+    model.load_inputs(dev_in["images"], dev_in["token_ids"], dev_in["state"], dev_in["noise"])
+    # count this library's launches in one eager forward
+    lib = _lib.load()
+    c0 = lib.vla_launch_count()
+    model.forward_device()
+    launches_per_step = lib.vla_launch_count() - c0
+    torch.cuda.synchronize()
+    model.capture()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        model.replay()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        model.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = max_over_ranks(ms, world)
+
+    # end to end through the public host API
+    out_host = torch.empty((B, cfg.expert.chunk, cfg.expert.action_dim), dtype=torch.float32, pin_memory=True)
+    for _ in range(2):
+        model.infer_host(host["images"], host["token_ids"], host["state"], host["noise"], out=out_host)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        model.infer_host(host["images"], host["token_ids"], host["state"], host["noise"], out=out_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall_e2e = (time.perf_counter() - t0) / args.steps * 1e3
+    barrier(world)
+    ms_e2e = max(e0.elapsed_time(e1) / args.steps, wall_e2e)
+    ms_e2e_max = max_over_ranks(ms_e2e, world)
+    clk = clocks.stop()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+    assert torch.isfinite(out_host).all(), "non-finite actions"
+
+    extras = {}
+    roofline = None
+    kernels = None
+    cpu_base = None
+    if rank == 0:
+        agg = profile_pass(model)
+        total_ms = sum(a["ms"] for a in agg.values())
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except (OSError, ValueError):
+            pass
+        tflops_peak = peaks.get("bf16_tflops_sustained") or 1400.0
+        hbm_peak = peaks.get("hbm_gbs") or 6650.0
+        peak_src = "measured" if peaks else "fallback"
+        kernels = {}
+        for k, a in sorted(agg.items(), key=lambda kv: -kv[1]["ms"]):
+            ent = {"launches": a["launches"], "ms_per_step": round(a["ms"], 4),
+                   "share": round(a["ms"] / total_ms, 4) if total_ms else None}
+            if a["flops"] > 0:
+                ach = a["flops"] / (a["ms"] * 1e-3) / 1e12
+                ent.update(achieved_tflops=round(ach, 1), frac_of_bf16_peak=round(ach / tflops_peak, 3))
+            if a["bytes"] > 0:
+                gbs = a["bytes"] / (a["ms"] * 1e-3) / 1e9
+                ent.update(achieved_gbs=round(gbs, 1), frac_of_hbm=round(gbs / hbm_peak, 3))
+            kernels[k] = ent
+        g = agg.get("gemm")
+        traffic = None
+        try:
+            prof = json.load(open(os.path.join(ROOT, "profiles", "gemm_traffic.json")))
+            traffic = prof.get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            pass
+        if g:
+            ach = g["flops"] / (g["ms"] * 1e-3) / 1e12
+            roofline = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel (all GEMM launches of one step)",
+                        "achieved": round(ach, 1), "peak": tflops_peak, "unit": "TFLOP/s",
+                        "frac": round(ach / tflops_peak, 4), "traffic": traffic,
+                        "peak_source": f"{peak_src} bf16_tflops_sustained",
+                        "launches_per_step": g["launches"],
+                        "algorithmic_flops_per_launch": g["flops"] / g["launches"],
+                        "avg_launch_ms": g["ms"] / g["launches"]}
+        if not args.no_extras and world == 1:
+            try:
+                extras["blocks"] = block_timings(torch)
+            except Exception as exc:  # extras never fail the benchmark line
+                extras["blocks_error"] = repr(exc)
+            sweep = {}
+            for b in (1, 8, 64):
+                model.allocate(b)
+                model.load_inputs(dev_in["images"][:b], dev_in["token_ids"][:b], dev_in["state"][:b],
+                                  dev_in["noise"][:b])
+                model.capture()
+                for _ in range(3):
+                    model.replay()
+                torch.cuda.synchronize()
+                a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 10
+                a_.record()
+                for _ in range(reps):
+                    model.replay()
+                b_.record()
+                b_.synchronize()
+                sweep[str(b)] = round(b / (a_.elapsed_time(b_) / reps / 1e3), 2)
+            sweep[str(B)] = round(B / (ms / 1e3), 2)
+            extras["batch_sweep_chunks_per_s"] = sweep
+            try:
+                n_obs = 2
+                sec, thr = cpu_chunk_seconds(n_obs, args.cpu_threads or os.cpu_count())
+                cpu_base = {"value": n_obs / sec, "unit": UNIT, "cores": thr, "kind": "port",
+                            "sample": f"{n_obs} observations (full action chunks, B=1 each) through the bf16 CPU "
+                                      "restatement of the reference's torch modules"}
+            except Exception as exc:
+                cpu_base = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "error": repr(exc)}
+
+    if rank == 0:
+        value = world * B / (ms_max / 1e3)
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights; images U(-1,1), token ids U[0,49152), state/noise N(0,1))",
+            "config": workload_config(args, B, world),
+            "e2e": {"value": round(world * B / (ms_e2e_max / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "note": "pinned host observations (bf16 images, int32 ids, bf16 state, fp32 noise) copied in, "
+                            "fp32 actions copied out, every step"},
+            "gpu_launches": int(launches_per_step) * args.steps,
+            "clocks": clk,
+            "roofline": roofline,
+            "kernels": kernels,
+            "cpu_baseline": cpu_base,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.kernel_case:
+        run_kernel_case(args)
+        return
+    if args.impl == "reference":
+        # the CPU reference path runs on rank 0 only; other ranks exit without work
+        run_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, world, local = dist_setup("nccl")
+    if world != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE {world}; using WORLD_SIZE")
+    run_ours(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

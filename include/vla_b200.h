@@ -92,6 +92,34 @@ int vla_peek_device_error(unsigned int* code);
 /* sizeof of the ABI structs, in the order vla_epilogue, vla_attention_args,
  * vla_llama_layer, vla_vision_layer, written to out[0..n); returns the count. */
 int vla_abi_sizes(int64_t* out, int32_t n);
+/* Number of kernel launches this library has issued in this process (all
+ * devices, all threads); a graph replay re-runs captured launches without
+ * counting them again. */
+uint64_t vla_launch_count(void);
+
+/* Launch profiler (measurement only; no counterpart in the reference, whose
+ * timing is the XRT host's "NPU execution time" print, gemm/v1_test_tiled_gemm.py:81-96).
+ * Between vla_profile_start and vla_profile_stop every launch of this library
+ * on this thread is bracketed by CUDA events; stop synchronises and returns one
+ * record per launch: its kind, device time and algorithmic FLOPs / bytes.
+ * Not for use during CUDA-graph capture. */
+enum {
+  VLA_KIND_GEMM = 0,
+  VLA_KIND_ATTENTION = 1,
+  VLA_KIND_NORM = 2,
+  VLA_KIND_ROPE = 3,
+  VLA_KIND_SOFTMAX = 4,
+  VLA_KIND_ELEMENTWISE = 5,
+  VLA_KIND_LAYOUT = 6
+};
+typedef struct vla_profile_record {
+  int32_t kind;
+  float ms;
+  double flops;
+  double bytes;
+} vla_profile_record;
+int vla_profile_start(int32_t capacity);
+int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count);
 
 /* ---------------------------------------------------------------------- */
 /* Per-op kernels (the reference's ExternalModule tops)                    */

@@ -29,12 +29,14 @@ static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const vo
                   "norm: 16-byte alignment");
   if (M == 0) return VLA_OK;
   const int grid = (int)((M + norm::kWarps - 1) / norm::kWarps);
+  prof_begin(st);
   if (mode == 0)
     norm::rownorm_kernel<0><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, nullptr,
                                                                  (bf16*)y, ldy, (int)M, (int)N, eps);
   else
     norm::rownorm_kernel<1><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, (const bf16*)b,
                                                                  (bf16*)y, ldy, (int)M, (int)N, eps);
+  prof_end(st, VLA_KIND_NORM, 0.0, 4.0 * (double)M * N);
   return launch_status("rownorm");
 }
 
@@ -48,7 +50,14 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st) {
                   "attention: 16-byte alignment of pointers and strides");
   if (batch == 0 || p.Lq == 0) return VLA_OK;
   dim3 grid((p.Lq + attn::BQ - 1) / attn::BQ, p.Hq, batch);
+  prof_begin(st);
   attn::flash_attn_kernel<<<grid, attn::kThreads, 0, st>>>(p);
+  {
+    const double lk = (double)p.Lk;
+    const double flops = 4.0 * batch * p.Hq * (double)p.Lq * lk * attn::HD;
+    const double bytes = 2.0 * batch * ((double)p.Lq * p.Hq * attn::HD * 2 + lk * p.Hkv * attn::HD * 2);
+    prof_end(st, VLA_KIND_ATTENTION, flops, bytes);
+  }
   return launch_status("flash_attn");
 }
 

@@ -45,7 +45,15 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const De
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
+  prof_begin(st);
   gemm_bf16_tc_kernel<BN><<<grid, kThreads, Cf::SMEM_BYTES, st>>>(ta, tb, ep, (int)M, (int)N, (int)K);
+  {
+    const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
+    double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
+    if (ep.residual) bytes += 2.0 * M * out_cols;
+    if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes);
+  }
   return launch_status("gemm_bf16_tc");
 }
 

@@ -4,10 +4,12 @@
 #pragma once
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "vla_b200.h"
@@ -97,7 +99,43 @@ static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, ui
 
 static inline cudaStream_t as_stream(vla_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Number of kernels this library has launched in this process.
+static std::atomic<unsigned long long> g_launch_count{0};
+
+// ---------------------------------------------------------------------------
+// Launch profiler: when enabled (never during graph capture), every launch is
+// bracketed by a CUDA event pair and tagged with its kind and algorithmic
+// FLOPs / bytes, so a caller can compute per-kernel roofline fractions.
+// ---------------------------------------------------------------------------
+struct ProfRec {
+  int kind;
+  double flops, bytes;
+  cudaEvent_t a, b;
+};
+struct Profiler {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  std::vector<ProfRec> recs;
+  size_t next = 0;
+  cudaEvent_t pending = nullptr;
+};
+static Profiler g_prof;
+
+static inline void prof_begin(cudaStream_t st) {
+  if (!g_prof.on || g_prof.next + 2 > g_prof.pool.size()) return;
+  g_prof.pending = g_prof.pool[g_prof.next++];
+  cudaEventRecord(g_prof.pending, st);
+}
+static inline void prof_end(cudaStream_t st, int kind, double flops, double bytes) {
+  if (!g_prof.on || g_prof.pending == nullptr || g_prof.next + 1 > g_prof.pool.size()) return;
+  cudaEvent_t e = g_prof.pool[g_prof.next++];
+  cudaEventRecord(e, st);
+  g_prof.recs.push_back(ProfRec{kind, flops, bytes, g_prof.pending, e});
+  g_prof.pending = nullptr;
+}
+
 static int launch_status(const char* what) {
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(VLA_E_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
   return VLA_OK;

@@ -33,6 +33,45 @@ int vla_peek_device_error(unsigned int* code) {
   return VLA_OK;
 }
 
+uint64_t vla_launch_count(void) { return g_launch_count.load(); }
+
+int vla_profile_start(int32_t capacity) {
+  VLA_CHECK_ARG(capacity > 0, "profile_start: capacity must be positive");
+  VLA_CHECK_ARG(!g_prof.on, "profile_start: profiler already running");
+  for (auto e : g_prof.pool) cudaEventDestroy(e);
+  g_prof.pool.assign(2 * (size_t)capacity, nullptr);
+  for (auto& e : g_prof.pool) VLA_CUDA_TRY(cudaEventCreate(&e));
+  g_prof.recs.clear();
+  g_prof.recs.reserve(capacity);
+  g_prof.next = 0;
+  g_prof.pending = nullptr;
+  g_prof.on = true;
+  return VLA_OK;
+}
+
+int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count) {
+  VLA_CHECK_ARG(g_prof.on, "profile_stop: profiler not running");
+  g_prof.on = false;
+  int n = 0;
+  for (const ProfRec& r : g_prof.recs) {
+    VLA_CUDA_TRY(cudaEventSynchronize(r.b));
+    if (out != nullptr && n < capacity) {
+      float ms = 0.f;
+      VLA_CUDA_TRY(cudaEventElapsedTime(&ms, r.a, r.b));
+      out[n].kind = r.kind;
+      out[n].ms = ms;
+      out[n].flops = r.flops;
+      out[n].bytes = r.bytes;
+    }
+    ++n;
+  }
+  if (count) *count = n;
+  for (auto e : g_prof.pool) cudaEventDestroy(e);
+  g_prof.pool.clear();
+  g_prof.recs.clear();
+  return VLA_OK;
+}
+
 int vla_abi_sizes(int64_t* out, int32_t n) {
   const int64_t sz[4] = {(int64_t)sizeof(vla_epilogue), (int64_t)sizeof(vla_attention_args),
                          (int64_t)sizeof(vla_llama_layer), (int64_t)sizeof(vla_vision_layer)};
@@ -66,7 +105,9 @@ int vla_rope_bf16(void* x, int64_t ld, int64_t M, int32_t ncols, int32_t seq, co
   VLA_CHECK_ALIGN(aligned16(x) && ld % 8 == 0, "rope: alignment");
   if (M == 0) return VLA_OK;
   const long long work = M * (ncols / 64) * 4;
+  prof_begin(as_stream(stream));
   ew::rope_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((bf16*)x, ld, M, ncols, seq, cs);
+  prof_end(as_stream(stream), VLA_KIND_ROPE, 0.0, 4.0 * (double)M * ncols);
   return launch_status("rope");
 }
 
@@ -90,8 +131,10 @@ int vla_softmax_bf16(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M
   VLA_CHECK_ARG(x && y && M >= 0 && N > 0 && ldx >= N && ldy >= N, "softmax: bad arguments");
   if (M == 0) return VLA_OK;
   const int wpb = 8;
+  prof_begin(as_stream(stream));
   ew::softmax_kernel<<<(int)((M + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(
       (const bf16*)x, ldx, (bf16*)y, ldy, (int)M, (int)N, scale, causal_row_start);
+  prof_end(as_stream(stream), VLA_KIND_SOFTMAX, 0.0, 4.0 * (double)M * N);
   return launch_status("softmax");
 }
 
@@ -103,8 +146,10 @@ int vla_elementwise_bf16(int32_t op, const void* x, int64_t ldx, const void* y2,
                       (op < 2 || ldy2 % 8 == 0),
                   "elementwise: alignment");
   if (M == 0) return VLA_OK;
+  prof_begin(as_stream(stream));
   ew::act_kernel<<<blocks::grid_for(M * (N / 8), 256), 256, 0, as_stream(stream)>>>(
       (const bf16*)x, ldx, (const bf16*)y2, ldy2, (bf16*)out, ldo, M, (int)N, op);
+  prof_end(as_stream(stream), VLA_KIND_ELEMENTWISE, 0.0, (op >= 2 ? 6.0 : 4.0) * (double)M * N);
   return launch_status("elementwise");
 }
 
@@ -142,8 +187,10 @@ int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, i
   VLA_CHECK_ALIGN(aligned16(in) && aligned16(out), "pixel_shuffle: alignment");
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * grid * grid * (C / 8);
+  prof_begin(as_stream(stream));
   ew::pixel_shuffle_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)in, (bf16*)out,
                                                                                        B, grid, scale, C);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * grid * grid * C);
   return launch_status("pixel_shuffle");
 }
 
@@ -154,8 +201,10 @@ int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, in
   VLA_CHECK_ALIGN(aligned16(img) && aligned16(out), "im2col: alignment");
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * (H / p) * (W / p) * (Cin * p * p / 8);
+  prof_begin(as_stream(stream));
   ew::im2col_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)img, (bf16*)out, B, Cin,
                                                                                 H, W, p);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * Cin * H * W);
   return launch_status("im2col");
 }
 
@@ -167,16 +216,20 @@ int vla_embed_bf16(const int32_t* ids, const void* table, int32_t vocab, int32_t
   VLA_CHECK_ALIGN(aligned16(table) && aligned16(out) && ldo % 8 == 0, "embed: alignment");
   if (B == 0 || T == 0) return VLA_OK;
   const long long work = (long long)B * T * (H / 8);
+  prof_begin(as_stream(stream));
   ew::embed_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>(
       ids, (const bf16*)table, vocab, H, B, T, scale, (bf16*)out, ldo, rows_per_seq, row_offset);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * T * H);
   return launch_status("embed");
 }
 
 int vla_f32_to_bf16(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t M, int64_t N, vla_stream_t stream) {
   VLA_CHECK_ARG(x && y && M >= 0 && N > 0 && ldx >= N && ldy >= N, "f32_to_bf16: bad arguments");
   if (M == 0) return VLA_OK;
+  prof_begin(as_stream(stream));
   ew::f32_to_bf16_kernel<<<blocks::grid_for(M * N, 256), 256, 0, as_stream(stream)>>>(x, ldx, (bf16*)y, ldy, M,
                                                                                       (int)N);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 6.0 * (double)M * N);
   return launch_status("f32_to_bf16");
 }
 

@@ -95,6 +95,15 @@ class VisionLayer(ctypes.Structure):
     ]
 
 
+class ProfileRecord(ctypes.Structure):
+    """Mirror of ``vla_profile_record``."""
+
+    _fields_ = [("kind", ctypes.c_int32), ("ms", ctypes.c_float), ("flops", ctypes.c_double),
+                ("bytes", ctypes.c_double)]
+
+
+KIND_NAMES = ["gemm", "attention", "norm", "rope", "softmax", "elementwise", "layout"]
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int
@@ -107,6 +116,9 @@ SIGNATURES = {
     "vla_sync_check": [],
     "vla_peek_device_error": [ctypes.POINTER(ctypes.c_uint)],
     "vla_abi_sizes": [ctypes.POINTER(ctypes.c_int64), _I32],
+    "vla_launch_count": [],
+    "vla_profile_start": [_I32],
+    "vla_profile_stop": [ctypes.POINTER(ProfileRecord), _I32, ctypes.POINTER(ctypes.c_int32)],
     "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
     "vla_gemm_bf16_tiled": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _P],
     "vla_rms_norm_bf16": [_P, _I64, _P, _P, _I64, _I64, _I64, _F32, _P],
@@ -127,7 +139,7 @@ SIGNATURES = {
     "vla_vision_layer_workspace": [ctypes.POINTER(VisionLayer), _I64],
     "vla_vision_layer_bf16": [ctypes.POINTER(VisionLayer), _P, _I32, _I32, _P, ctypes.c_size_t, _P],
 }
-_RET = {"vla_last_error": ctypes.c_char_p, "vla_llama_layer_workspace": ctypes.c_size_t,
+_RET = {"vla_last_error": ctypes.c_char_p, "vla_launch_count": ctypes.c_uint64, "vla_llama_layer_workspace": ctypes.c_size_t,
         "vla_vision_layer_workspace": ctypes.c_size_t}
 
 EW_GELU_TANH = 0

@@ -289,6 +289,19 @@ class SmolVLA:
         self.in_state.copy_(state.to(BF16) if state.dtype != BF16 else state, non_blocking=non_blocking)
         self.in_noise.copy_(noise.reshape(B * self.cfg.expert.chunk, -1), non_blocking=non_blocking)
 
+    def infer_host(self, images, token_ids, state, noise, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """End-to-end call from host memory: copy the observations in (pinned host
+        buffers give asynchronous copies), replay the chunk graph, copy the actions
+        [B, chunk, action_dim] fp32 back to ``out`` (pinned host) and wait for it."""
+        self.load_inputs(images, token_ids, state, noise, non_blocking=True)
+        res = self.replay()
+        if out is None:
+            out = torch.empty((self.batch, self.cfg.expert.chunk, self.cfg.expert.action_dim), dtype=torch.float32,
+                              pin_memory=True)
+        out.view(-1, self.cfg.expert.action_dim).copy_(res, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
     def infer(self, images, token_ids, state, noise, use_graph: bool = True) -> torch.Tensor:
         """Action chunks [B, chunk, action_dim] (fp32) for a batch of observations."""
         self.load_inputs(images, token_ids, state, noise)
