@@ -23,7 +23,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter, splitting the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-blocks sweep all N-blocks
 
 struct DevEpi {
@@ -118,13 +119,16 @@ __device__ __forceinline__ void finish16(const DevEpi& ep, int m, int n, long lo
   cp[1] = pack_bf16x8(v + 8);
 }
 
+// Epilogue of one 128 x BN accumulator tile for one row m; warps that share a
+// lane quarter split the column chunks round-robin (part of nparts).
 template <int BN>
-__device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0) {
+__device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, int part,
+                                              int nparts) {
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
 #pragma unroll 1
-    for (int h = 0; h < BN; h += 64) {
+    for (int h = 64 * part; h < BN; h += 64 * nparts) {
       float x[64];
 #pragma unroll
       for (int j = 0; j < 4; ++j) tmem_ld16(taddr + h + 16 * j, x + 16 * j);
@@ -169,7 +173,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
     }
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 32 * part; c < BN; c += 32 * nparts) {
       float g[16], u[16];
       tmem_ld16(taddr + c, g);
       tmem_ld16(taddr + c + 16, u);
@@ -193,17 +197,21 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
     }
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(taddr + c, v);
-      const int n = n0 + c;
-      if (n >= ep.N) continue;
+    for (int c = 32 * part; c < BN; c += 32 * nparts) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] *= ep.alpha;
-      finish16(ep, m, n, orow, v, row_ok);
+      for (int half = 0; half < 2; ++half) {
+        float v[16];
+        tmem_ld16(taddr + c + 16 * half, v);
+        const int n = n0 + c + 16 * half;
+        if (n >= ep.N) continue;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= ep.alpha;
+        finish16(ep, m, n, orow, v, row_ok);
+      }
     }
   }
 }
+
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 32 * kEpiWarps);
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -320,7 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int part = (warp - 2) >> 2;     // which column share of that quarter
     int tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mb, nb;
@@ -339,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = mb * BM + q * 32 + lane;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4);
       tc_fence_before();
       mbar_arrive(&tempty[as]);
       ++tc;
