@@ -275,6 +275,31 @@ int vla_llama_cross_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch,
                                const void* k, const void* v, int64_t ldkv, int32_t kv_seq, const int32_t* kv_len,
                                void* workspace, size_t workspace_bytes, vla_stream_t stream);
 
+/* Allocation-free variant of vla_llama_self_layer_bf16.  It has no
+ * counterpart in the reference; it exists for callers that cannot allocate
+ * device memory — a real-time control loop that must not call cudaMalloc
+ * mid-episode, a host framework or plugin sandbox that owns every device
+ * buffer and hands out only inputs and outputs, or an FFI binding with no
+ * CUDA allocator of its own.  Such a caller passes x (and optionally
+ * qkv_out) as before but no workspace: the layer's scratch lives in one
+ * static device array of VLA_NOALLOC_SCRATCH_BYTES inside the library,
+ * which every GPU that loads the library holds until the process exits.
+ * - A request whose workspace would exceed that size is rejected with
+ *   VLA_E_WORKSPACE before any launch (at the 960-wide text-layer shape the
+ *   limit is 689 rows = batch * seq, or 936 rows when qkv_out is given).
+ *   The call itself allocates nothing.
+ * - The first call on each device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture on the device.
+ * - All calls share the one array and it keeps the previous call's
+ *   contents (nothing in it needs to start at zero).  Two calls whose
+ *   kernels overlap on the GPU (different streams, or different host
+ *   threads on one device) race on it: serialise them. */
+#define VLA_NOALLOC_SCRATCH_BYTES (8u << 20)
+size_t vla_noalloc_scratch_bytes(void);
+int vla_llama_self_layer_bf16_noalloc(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq,
+                                      const float* rope_cs, void* qkv_out, vla_stream_t stream);
+
 /* SigLIP encoder layer weights (K-major): w_qkv = [Wq | Wk | Wv]^T [3 hidden, hidden],
  * b_qkv [3 hidden], w_o [hidden, hidden], w_fc1 [ffn, hidden], w_fc2 [hidden, ffn]. */
 typedef struct vla_vision_layer {

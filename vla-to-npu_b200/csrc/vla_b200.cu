@@ -10,6 +10,36 @@
 
 using namespace vla;
 
+// Scratch of vla_llama_self_layer_bf16_noalloc: one fixed array in device
+// memory, present on every device that loads this library.  Host code may
+// not use the symbol itself as a device address; it looks the address up
+// once per device (noalloc_scratch below).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[VLA_NOALLOC_SCRATCH_BYTES];
+
+static void* noalloc_scratch(int* rc) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = set_error(VLA_E_CUDA, "noalloc: cudaGetDevice failed");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *rc = set_error(VLA_E_CUDA, "noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                      cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *rc = VLA_OK;
+  return addr[dev];
+}
+
 extern "C" {
 
 const char* vla_last_error(void) { return t_last_error; }
@@ -248,6 +278,25 @@ int vla_llama_cross_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch,
                                void* workspace, size_t workspace_bytes, vla_stream_t stream) {
   return blocks::llama_cross(w, x, batch, seq, rope_cs, k, v, ldkv, kv_seq, kv_len, workspace, workspace_bytes,
                              as_stream(stream));
+}
+
+size_t vla_noalloc_scratch_bytes(void) { return VLA_NOALLOC_SCRATCH_BYTES; }
+
+int vla_llama_self_layer_bf16_noalloc(const vla_llama_layer* w, void* x, int32_t batch, int32_t seq,
+                                      const float* rope_cs, void* qkv_out, vla_stream_t stream) {
+  VLA_CHECK_ARG(w != nullptr && batch >= 0 && seq > 0, "noalloc llama self: bad arguments");
+  const int64_t rows = (int64_t)batch * seq;
+  const size_t need = blocks::llama_ws_bytes(w, rows, qkv_out == nullptr);
+  if (need > VLA_NOALLOC_SCRATCH_BYTES)
+    return set_error(VLA_E_WORKSPACE,
+                     "noalloc llama self: %lld rows need %zu bytes of scratch, above the fixed %u-byte static array; "
+                     "use vla_llama_self_layer_bf16 with a caller workspace",
+                     (long long)rows, need, (unsigned)VLA_NOALLOC_SCRATCH_BYTES);
+  int rc = VLA_OK;
+  void* scratch = noalloc_scratch(&rc);
+  if (scratch == nullptr) return rc;
+  return blocks::llama_self(w, x, batch, seq, rope_cs, qkv_out, scratch, VLA_NOALLOC_SCRATCH_BYTES,
+                            as_stream(stream));
 }
 
 size_t vla_vision_layer_workspace(const vla_vision_layer* w, int64_t rows) {

@@ -137,10 +137,12 @@ SIGNATURES = {
     "vla_llama_cross_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, _I64, _I32, _P, _P,
                                    ctypes.c_size_t, _P],
     "vla_vision_layer_workspace": [ctypes.POINTER(VisionLayer), _I64],
+    "vla_noalloc_scratch_bytes": [],
+    "vla_llama_self_layer_bf16_noalloc": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P],
     "vla_vision_layer_bf16": [ctypes.POINTER(VisionLayer), _P, _I32, _I32, _P, ctypes.c_size_t, _P],
 }
 _RET = {"vla_last_error": ctypes.c_char_p, "vla_launch_count": ctypes.c_uint64, "vla_llama_layer_workspace": ctypes.c_size_t,
-        "vla_vision_layer_workspace": ctypes.c_size_t}
+        "vla_vision_layer_workspace": ctypes.c_size_t, "vla_noalloc_scratch_bytes": ctypes.c_size_t}
 
 EW_GELU_TANH = 0
 EW_SILU = 1
