@@ -259,7 +259,7 @@ def run_reference(args, rank, world):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights and observations)",
-        "config": workload_config(args, 1, 1),
+        "config": workload_config(args, args.batch, world),
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
@@ -297,6 +297,7 @@ def profile_pass(model) -> dict:
     n = ctypes.c_int32(0)
     _lib.call("vla_profile_stop", recs, cap, ctypes.byref(n))
     agg = {}
+    shapes = {}
     for i in range(min(n.value, cap)):
         r = recs[i]
         k = _lib.KIND_NAMES[r.kind]
@@ -305,7 +306,15 @@ def profile_pass(model) -> dict:
         a["ms"] += r.ms
         a["flops"] += r.flops
         a["bytes"] += r.bytes
+        if r.kind == 0:
+            sh = shapes.setdefault((r.m, r.n, r.k), [0, 0.0, 0.0])
+            sh[0] += 1
+            sh[1] += r.ms
+            sh[2] += r.flops
     del lib
+    top = sorted(shapes.items(), key=lambda kv: -kv[1][1])[:12]
+    agg["_gemm_shapes"] = [{"mnk": list(s), "launches": v[0], "ms": round(v[1], 3),
+                            "tflops": round(v[2] / (v[1] * 1e-3) / 1e12, 1)} for s, v in top]
     return agg
 
 
@@ -426,6 +435,7 @@ def run_ours(args, rank, world, local):
     cpu_base = None
     if rank == 0:
         agg = profile_pass(model)
+        extras["gemm_shapes"] = agg.pop("_gemm_shapes")
         total_ms = sum(a["ms"] for a in agg.values())
         peaks = {}
         try:

@@ -117,6 +117,7 @@ typedef struct vla_profile_record {
   float ms;
   double flops;
   double bytes;
+  int64_t m, n, k; /* GEMM problem shape (0 for other kinds) */
 } vla_profile_record;
 int vla_profile_start(int32_t capacity);
 int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count);
@@ -136,7 +137,7 @@ int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count);
 int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
                   int64_t K, const vla_epilogue* epi, vla_stream_t stream);
 
-/* Same GEMM with the N tile width forced (32, 64, 128 or 256) instead of chosen
+/* Same GEMM with the N tile width forced (a multiple of 32 in [32, 256]) instead of chosen
  * by the launcher's wave-count heuristic; used by tests and tile sweeps. */
 int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
                         int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, vla_stream_t stream);
@@ -204,7 +205,14 @@ typedef struct vla_attention_args {
   int32_t causal;
   const int32_t* kv_len; /* device int32 [batch] or NULL */
   float scale;
+  int32_t impl;          /* VLA_ATTN_AUTO, VLA_ATTN_MMA_SYNC or VLA_ATTN_TCGEN05 */
 } vla_attention_args;
+/* Attention kernels: AUTO picks the tcgen05 kernel (persistent, 128-row query
+ * tiles, TMEM accumulators) for non-causal attention with Lk >= 256 and the
+ * mma.sync kernel (64-row tiles) otherwise; TCGEN05 supports non-causal
+ * attention only and needs q_batch / k_batch / v_batch to be whole multiples of
+ * the row strides. */
+enum { VLA_ATTN_AUTO = 0, VLA_ATTN_MMA_SYNC = 1, VLA_ATTN_TCGEN05 = 2 };
 int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream);
 
 /* Pixel shuffle: in [B, grid*grid, C] -> out [B, (grid/s)^2, s*s*C] with

@@ -214,3 +214,45 @@ def test_bad_arguments_raise(cuda):
     with pytest.raises(_lib.VlaError) as e:
         dev.gemm(a, w, out[:, :20])  # N = 20 not a multiple of 16
     assert e.value.code == _lib.VLA_E_INVALID
+
+
+@pytest.mark.parametrize("Lq,Lk,Hq,Hkv,B,kv_len", [
+    (1024, 1024, 12, 12, 2, None),   # SigLIP (C1): 8 query tiles x 8 key tiles
+    (200, 300, 4, 4, 2, None),       # ragged query and key tails
+    (128, 256, 15, 5, 1, None),      # GQA 3:1
+    (50, 113, 15, 5, 3, [113, 60, 1]),  # expert cross shape with key padding
+])
+def test_attention_tcgen05(cuda, Lq, Lk, Hq, Hkv, B, kv_len):
+    """The tcgen05 flash-attention kernel (TMEM accumulators, P from smem, V as an
+    MN-major operand) forced on, against the fp32 oracle."""
+    from vla_b200 import _lib, device as dev
+    q = _rand((B, Lq, Hq, 64), 21)
+    k = _rand((B, Lk, Hkv, 64), 22)
+    v = _rand((B, Lk, Hkv, 64), 23)
+    o = torch.full((B * Lq, Hq * 64), float("nan"), dtype=BF, device="cuda")
+    kl = None if kv_len is None else torch.tensor(kv_len, dtype=torch.int32, device="cuda")
+    dev.attention(q.reshape(B * Lq, -1).cuda(), k.reshape(B * Lk, -1).cuda(), v.reshape(B * Lk, -1).cuda(), o,
+                  batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=Lq * Hq * 64, k_batch=Lk * Hkv * 64,
+                  v_batch=Lk * Hkv * 64, o_batch=Lq * Hq * 64, kv_len=kl, impl=_lib.ATTN_TCGEN05)
+    dev.sync_check()
+    ref = R.attention(q, k, v, causal=False, kv_len=kv_len, dt=torch.float32).reshape(B * Lq, -1)
+    torch.testing.assert_close(o.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_attention_tcgen05_strided_qkv(cuda):
+    """Q/K/V as column views of one fused QKV buffer (the SigLIP layer layout), more
+    work items than SMs so each persistent CTA walks several items."""
+    from vla_b200 import _lib, device as dev
+    B, L, H = 20, 1024, 12
+    qkv = _rand((B * L, 3 * H * 64), 24)
+    qd = qkv.cuda()
+    o = torch.empty(B * L, H * 64, dtype=BF, device="cuda")
+    dev.attention(qd[:, :H * 64], qd[:, H * 64:2 * H * 64], qd[:, 2 * H * 64:], o, batch=B, Lq=L, Lk=L, Hq=H,
+                  Hkv=H, q_batch=L * 3 * H * 64, k_batch=L * 3 * H * 64, v_batch=L * 3 * H * 64, o_batch=L * H * 64,
+                  impl=_lib.ATTN_TCGEN05)
+    dev.sync_check()
+    x = qkv.view(B, L, 3, H, 64)
+    for b in (0, B - 1):
+        ref = R.attention(x[b:b + 1, :, 0], x[b:b + 1, :, 1], x[b:b + 1, :, 2], causal=False,
+                          dt=torch.float32).reshape(L, -1)
+        torch.testing.assert_close(o[b * L:(b + 1) * L].float().cpu(), ref, atol=2e-2, rtol=2e-2)

@@ -1,0 +1,375 @@
+// Flash attention on the 5th-generation tensor cores (tcgen05), head_dim 64.
+//
+// Work item = 128 query rows of one (sequence, head); a persistent CTA per SM
+// walks the work items.  Warp roles:
+//   warp 0     TMA producer: Q (double-buffered across items), K and V tiles of
+//              128 keys into separate 3-stage rings (K is released as soon as
+//              S = Q K^T completes, V after P.V)
+//   warp 1     TMEM allocator + single-thread MMA issuer:
+//                S_j  = Q . K_j^T   (UMMA 128x128x16, A = Q, B = K, both K-major)
+//                PV_j = P_j . V_j   (UMMA 128x64x16, A = P from smem K-major,
+//                                    B = V from smem MN-major, no transpose pass)
+//   warps 2..5 softmax: thread r owns query row r; reads its S row from TMEM
+//              (so row max / sum need no shuffles), P = exp2(S*scale*log2e - m)
+//              rounded to bf16 into swizzled smem for the P.V MMA, and keeps the
+//              output row O (64 fp32) in registers: O = O*alpha + PV.
+// S is double-buffered in TMEM (S_{j+1} is computed while row j is in softmax),
+// P and PV are double-buffered too.  TMEM: 2 x 128 (S) + 2 x 64 (PV) columns.
+//
+// Used for the non-causal SigLIP attention (1024 keys per head); the small
+// text / expert attentions run on the mma.sync kernel (attention.cuh).
+#pragma once
+#include "common.cuh"
+
+namespace vla {
+namespace attn_tc {
+
+constexpr int BQ = 128;   // query rows per work item (UMMA M)
+constexpr int BKV = 128;  // keys per tile (UMMA N of S, K of P.V)
+constexpr int HD = 64;
+constexpr int kKStages = 3;
+constexpr int kVStages = 3;
+constexpr int kThreads = 192;
+constexpr int TILE_BYTES = BKV * HD * 2;  // 16 KB: a [128 x 64] bf16 tile (Q, K or V)
+constexpr int P_BYTES = BQ * BKV * 2;     // 32 KB: P as two [128 x 64] swizzled atoms
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL0 = 0;     // S buffers at columns 0 and 128
+constexpr uint32_t PV_COL0 = 256;  // PV buffers at columns 256 and 320
+
+struct Params {
+  int Lq, Lk, Hq, Hkv, batch;
+  int n_qt;                                  // query tiles per (sequence, head)
+  long long q_rows_per_seq, k_rows_per_seq;  // row offset of sequence b = b * rows_per_seq
+  bf16* o;
+  long long o_row, o_batch;
+  const int* kv_len;
+  float scale_log2;
+};
+
+struct Smem {
+  uint8_t q[2][TILE_BYTES];
+  uint8_t k[kKStages][TILE_BYTES];
+  uint8_t v[kVStages][TILE_BYTES];
+  uint8_t p[2][P_BYTES];
+  uint64_t q_full[2], q_empty[2];
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t s_full[2], p_full[2], pv_full[2], pv_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// MN-major SW128 descriptor for a [rows x 64] bf16 tile read along the row
+// (K) direction: 8-row groups 1024 bytes apart (stride byte offset), a single
+// 64-element atom along N.
+__device__ __forceinline__ uint64_t make_sw128_mn_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(16384u >> 4) << 16;  // leading byte offset: next N atom (unused for N = 64)
+  d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset: next 8 K-rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// work item w -> (query tile, head, sequence); consecutive items share K/V
+__device__ __forceinline__ void item_coords(const Params& p, int w, int& qt, int& h, int& b) {
+  qt = w % p.n_qt;
+  h = (w / p.n_qt) % p.Hq;
+  b = w / (p.n_qt * p.Hq);
+}
+
+__device__ __forceinline__ int item_keys(const Params& p, int b) {
+  int Lk = p.Lk;
+  if (p.kv_len != nullptr) Lk = min(Lk, __ldg(p.kv_len + b));
+  return max(Lk, 0);
+}
+
+// Persistent kernel: CTA i processes work items i, i + gridDim.x, ...  Every
+// pipeline counter (K/V ring slots, S/P/PV buffers) runs over the CTA's global
+// tile index, so loads and MMAs of the next item overlap the tail of this one.
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_items = p.n_qt * p.Hq * p.batch;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.q_full[i], 1);
+      mbar_init(&sm.q_empty[i], 1);
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.p_full[i], 128);
+      mbar_init(&sm.pv_full[i], 1);
+      mbar_init(&sm.pv_empty[i], 128);
+    }
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    sm.abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      bool ok = true;
+      int tk = 0, tv = 0, it = 0;  // K / V tiles issued, items started
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+        int qt, h, b;
+        item_coords(p, w, qt, h, b);
+        const int kvh = (int)((long long)h * p.Hkv / p.Hq);
+        const int n = (item_keys(p, b) + BKV - 1) / BKV;
+        const int qb = it & 1;
+        if (!mbar_wait_bounded(&sm.q_empty[qb], ((it >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.q_full[qb], TILE_BYTES);
+        tma_load_2d(sm.q[qb], &tmQ, &sm.q_full[qb], h * HD, (int)(b * p.q_rows_per_seq) + qt * BQ);
+        const int k_row0 = (int)(b * p.k_rows_per_seq);
+        for (int j = 0; j < n; ++j) {
+          const int sk = tk % kKStages;
+          if (!mbar_wait_bounded(&sm.k_empty[sk], ((tk / kKStages) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.k_full[sk], TILE_BYTES);
+          tma_load_2d(sm.k[sk], &tmK, &sm.k_full[sk], kvh * HD, k_row0 + j * BKV);
+          ++tk;
+          const int sv = tv % kVStages;
+          if (!mbar_wait_bounded(&sm.v_empty[sv], ((tv / kVStages) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.v_full[sv], TILE_BYTES);
+          tma_load_2d(sm.v[sv], &tmV, &sm.v_full[sv], kvh * HD, k_row0 + j * BKV);
+          ++tv;
+        }
+      }
+      if (!ok) {
+        if (!*abort_flag) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // let issued copies land before the CTA can exit
+      for (int i = (tk > kKStages ? tk - kKStages : 0); i < tk; ++i)
+        mbar_wait_bounded(&sm.k_full[i % kKStages], (i / kKStages) & 1, nullptr, 20000000ull);
+      for (int i = (tv > kVStages ? tv - kVStages : 0); i < tv; ++i)
+        mbar_wait_bounded(&sm.v_full[i % kVStages], (i / kVStages) & 1, nullptr, 20000000ull);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, HD) | (1u << 16);  // B (V) is MN-major
+      bool ok = true;
+      int t = 0, it = 0;
+      for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
+        int qt, h, b;
+        item_coords(p, w, qt, h, b);
+        const int n = (item_keys(p, b) + BKV - 1) / BKV;
+        const int qb = it & 1;
+        ok = mbar_wait_bounded(&sm.q_full[qb], (it >> 1) & 1, abort_flag);
+        const uint64_t qdesc = make_sw128_desc(smem_u32(sm.q[qb]));
+        // S of tile j, then P.V of tile j-1; finally P.V of the item's last tile
+        for (int j = 0; ok && j <= n; ++j) {
+          if (j < n) {
+            const int tt = t + j;
+            const int sk = tt % kKStages;
+            ok = mbar_wait_bounded(&sm.k_full[sk], (tt / kKStages) & 1, abort_flag);
+            // S buffer tt%2 was last read by the softmax of tile tt-2 (released with P_{tt-2})
+            if (ok && tt >= 2) ok = mbar_wait_bounded(&sm.p_full[tt & 1], ((tt - 2) >> 1) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t kdesc = make_sw128_desc(smem_u32(sm.k[sk]));
+            const uint32_t d = tmem + S_COL0 + (uint32_t)(tt & 1) * BKV;
+#pragma unroll
+            for (int k = 0; k < HD / 16; ++k) tc_mma_bf16(d, qdesc + 2 * k, kdesc + 2 * k, idesc_s, k > 0);
+            tc_commit(&sm.s_full[tt & 1]);
+            tc_commit(&sm.k_empty[sk]);
+          }
+          if (j >= 1) {
+            const int tp = t + j - 1;
+            const int sv = tp % kVStages;
+            ok = mbar_wait_bounded(&sm.p_full[tp & 1], (tp >> 1) & 1, abort_flag);
+            if (ok && tp >= 2) ok = mbar_wait_bounded(&sm.pv_empty[tp & 1], ((tp - 2) >> 1) & 1, abort_flag);
+            if (ok) ok = mbar_wait_bounded(&sm.v_full[sv], (tp / kVStages) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t pbase = smem_u32(sm.p[tp & 1]);
+            const uint32_t vbase = smem_u32(sm.v[sv]);
+            const uint32_t d = tmem + PV_COL0 + (uint32_t)(tp & 1) * HD;
+#pragma unroll
+            for (int k = 0; k < BKV / 16; ++k) {
+              const uint64_t adesc =
+                  make_sw128_desc(pbase + (uint32_t)(k >> 2) * 16384u + (uint32_t)(k & 3) * 32u);
+              const uint64_t bdesc = make_sw128_mn_desc(vbase + (uint32_t)k * 2048u);
+              tc_mma_bf16(d, adesc, bdesc, idesc_pv, k > 0);
+            }
+            tc_commit(&sm.pv_full[tp & 1]);
+            tc_commit(&sm.v_empty[sv]);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&sm.q_empty[qb]);  // every S of this item has been issued before this point
+        t += n;
+      }
+      if (!ok) {
+        if (!*abort_flag) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    // ---------------- softmax / output warps ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    bool ok = true;
+    int t = 0;
+    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+      int qt, h, b;
+      item_coords(p, w, qt, h, b);
+      const int Lk = item_keys(p, b);
+      const int n = (Lk + BKV - 1) / BKV;
+      float o[HD];
+#pragma unroll
+      for (int i = 0; i < HD; ++i) o[i] = 0.f;
+      float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+      for (int j = 0; j <= n; ++j) {
+        float alpha = 1.f;
+        if (j < n) {
+          const int tt = t + j;
+          ok = mbar_wait_bounded(&sm.s_full[tt & 1], (tt >> 1) & 1, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sadr = tmem + lane_base + S_COL0 + (uint32_t)(tt & 1) * BKV;
+          const int key0 = j * BKV;
+          float s[BKV];
+#pragma unroll
+          for (int c = 0; c < BKV; c += 32) tmem_ld32(sadr + c, s + c);
+          float mx = -INFINITY;
+          if (key0 + BKV <= Lk) {
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+              s[c] *= p.scale_log2;
+              mx = fmaxf(mx, s[c]);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < BKV; ++c) {
+              s[c] = (key0 + c < Lk) ? s[c] * p.scale_log2 : -INFINITY;
+              mx = fmaxf(mx, s[c]);
+            }
+          }
+          const float mnew = fmaxf(m, mx);
+          const float mbase = mnew == -INFINITY ? 0.f : mnew;
+          alpha = ex2_fast(m - mbase);
+          m = mnew;
+          float rs = 0.f;
+          // P row (128 keys, bf16) into the two swizzled 64-key atoms of P buffer tt%2
+          uint8_t* prow = sm.p[tt & 1] + row * 128;
+#pragma unroll
+          for (int c8 = 0; c8 < BKV / 8; ++c8) {
+            float e[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              e[i] = ex2_fast(s[c8 * 8 + i] - mbase);
+              rs += e[i];
+            }
+            const int atom = c8 >> 3, chunk = c8 & 7;
+            *reinterpret_cast<uint4*>(prow + atom * 16384 + ((chunk ^ (row & 7)) << 4)) = pack_bf16x8(e);
+          }
+          l = l * alpha + rs;
+          // make the generic-proxy smem writes of P visible to the tensor core
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tc_fence_before();
+          mbar_arrive(&sm.p_full[tt & 1]);
+        }
+        if (j >= 1) {
+          const int tp = t + j - 1;
+          ok = mbar_wait_bounded(&sm.pv_full[tp & 1], (tp >> 1) & 1, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t padr = tmem + lane_base + PV_COL0 + (uint32_t)(tp & 1) * HD;
+          float pv[HD];
+          tmem_ld32(padr, pv);
+          tmem_ld32(padr + 32, pv + 32);
+          tc_fence_before();
+          mbar_arrive(&sm.pv_empty[tp & 1]);
+#pragma unroll
+          for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + pv[i];
+        }
+        alpha_prev = alpha;
+      }
+      if (!ok) break;
+      const int qrow = qt * BQ + row;
+      if (qrow < p.Lq) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.o + (long long)b * p.o_batch + (long long)qrow * p.o_row +
+                                              (long long)h * HD);
+#pragma unroll
+        for (int c8 = 0; c8 < HD / 8; ++c8) {
+          float tv8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) tv8[i] = o[c8 * 8 + i] * inv;
+          dst[c8] = pack_bf16x8(tv8);
+        }
+      }
+      t += n;
+    }
+    if (!ok && lane == 0) {
+      if (!*abort_flag) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace attn_tc
+}  // namespace vla

@@ -3,6 +3,7 @@
 // lives in a caller-provided workspace (no allocation here).
 #pragma once
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "elementwise.cuh"
 #include "gemm_host.cuh"
 #include "norm.cuh"
@@ -40,15 +41,72 @@ static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const vo
   return launch_status("rownorm");
 }
 
-static int attention(const attn::Params& p, int batch, cudaStream_t st) {
+// tcgen05 attention: persistent CTAs over (query tile, head, sequence) items
+static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
+  VLA_CHECK_ARG(!p.causal, "attention (tcgen05): causal masking is not supported");
+  VLA_CHECK_ARG(p.q_batch % p.q_row == 0 && p.k_batch % p.k_row == 0 && p.v_batch % p.v_row == 0 &&
+                    p.k_batch / p.k_row == p.v_batch / p.v_row,
+                "attention (tcgen05): sequence strides must be whole rows, equal for K and V");
+  const long long q_rows = p.q_batch / p.q_row, k_rows = p.k_batch / p.k_row;
+  const long long total_q = (batch - 1) * q_rows + p.Lq, total_k = (batch - 1) * k_rows + p.Lk;
+  VLA_CHECK_ARG(total_q < (1ll << 31) && total_k < (1ll << 31), "attention (tcgen05): too many rows");
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_bf16_2d(&tq, p.q, (uint64_t)p.Hq * 64, (uint64_t)total_q, (uint64_t)p.q_row, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tk, p.k, (uint64_t)p.Hkv * 64, (uint64_t)(total_k > 0 ? total_k : 1), (uint64_t)p.k_row,
+                         64, 128);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tv, p.v, (uint64_t)p.Hkv * 64, (uint64_t)(total_k > 0 ? total_k : 1), (uint64_t)p.v_row,
+                         64, 128);
+  if (rc) return rc;
+  attn_tc::Params tp{};
+  tp.Lq = p.Lq;
+  tp.Lk = p.Lk;
+  tp.Hq = p.Hq;
+  tp.Hkv = p.Hkv;
+  tp.batch = batch;
+  tp.n_qt = (p.Lq + attn_tc::BQ - 1) / attn_tc::BQ;
+  tp.q_rows_per_seq = q_rows;
+  tp.k_rows_per_seq = k_rows;
+  tp.o = p.o;
+  tp.o_row = p.o_row;
+  tp.o_batch = p.o_batch;
+  tp.kv_len = p.kv_len;
+  tp.scale_log2 = p.scale_log2;
+  const int smem = (int)sizeof(attn_tc::Smem) + 1024;
+  static thread_local int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(
+        cudaFuncSetAttribute(attn_tc::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const long long items = (long long)tp.n_qt * p.Hq * batch;
+  VLA_CHECK_ARG(items < (1ll << 31), "attention (tcgen05): too many work items");
+  const int sms = device_info().num_sms;
+  const int grid = (int)(items < sms ? items : sms);
+  prof_begin(st);
+  attn_tc::flash_attn_tc_kernel<<<grid, attn_tc::kThreads, smem, st>>>(tq, tk, tv, tp);
+  prof_end(st, VLA_KIND_ATTENTION, 4.0 * batch * p.Hq * (double)p.Lq * p.Lk * 64,
+           2.0 * batch * ((double)p.Lq * p.Hq * 64 * 2 + (double)p.Lk * p.Hkv * 64 * 2));
+  return launch_status("flash_attn_tc");
+}
+
+static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl = VLA_ATTN_AUTO) {
   VLA_CHECK_ARG(p.q && p.k && p.v && p.o, "attention: null pointer");
   VLA_CHECK_ARG(batch >= 0 && p.Lq >= 0 && p.Lk >= 0 && p.Hq > 0 && p.Hkv > 0 && p.Hq % p.Hkv == 0,
                 "attention: bad shape");
+  VLA_CHECK_ARG(p.q_row > 0 && p.k_row > 0 && p.v_row > 0 && p.o_row > 0, "attention: row strides must be positive");
   VLA_CHECK_ALIGN(aligned16(p.q) && aligned16(p.k) && aligned16(p.v) && aligned16(p.o) && p.q_row % 8 == 0 &&
                       p.k_row % 8 == 0 && p.v_row % 8 == 0 && p.o_row % 8 == 0 && p.q_batch % 8 == 0 &&
                       p.k_batch % 8 == 0 && p.v_batch % 8 == 0 && p.o_batch % 8 == 0,
                   "attention: 16-byte alignment of pointers and strides");
   if (batch == 0 || p.Lq == 0) return VLA_OK;
+  if (impl == VLA_ATTN_TCGEN05 || (impl == VLA_ATTN_AUTO && !p.causal && p.Lk >= 256 &&
+                                   p.q_batch % p.q_row == 0 && p.k_batch % p.k_row == 0 &&
+                                   p.v_batch % p.v_row == 0 && p.k_batch / p.k_row == p.v_batch / p.v_row))
+    return attention_tc(p, batch, st);
   dim3 grid((p.Lq + attn::BQ - 1) / attn::BQ, p.Hq, batch);
   prof_begin(st);
   attn::flash_attn_kernel<<<grid, attn::kThreads, 0, st>>>(p);

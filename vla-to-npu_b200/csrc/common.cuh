@@ -22,6 +22,7 @@ enum : unsigned int {
   VLA_DERR_GEMM_PRODUCER_TIMEOUT = 0x101,
   VLA_DERR_GEMM_MMA_TIMEOUT = 0x102,
   VLA_DERR_GEMM_EPILOGUE_TIMEOUT = 0x103,
+  VLA_DERR_ATTN_TIMEOUT = 0x201,
   VLA_DERR_TEST_TIMEOUT = 0x1FF,
 };
 

@@ -52,10 +52,10 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN <= 64) ? 8 : (BN <= 128 ? 6 : 4);
+  static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) > 8 ? 8 : (200 * 1024 / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
-  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (multiple of 32 for the epilogue chunks)");
   static_assert(B_BYTES % 1024 == 0, "B tile alignment");
 };
 
@@ -74,25 +74,61 @@ __device__ __forceinline__ long long out_row(const DevEpi& ep, int m) {
   return m;
 }
 
-// Finish 16 consecutive columns [n, n+16) of row m held in v[] (fp32).
-__device__ __forceinline__ void finish16(const DevEpi& ep, int m, int n, long long orow, float* v, bool row_ok) {
-  if (ep.bias != nullptr) {
-    float b[16];
-    const uint4* bp = reinterpret_cast<const uint4*>(ep.bias + n);
-    unpack_bf16x8(__ldg(bp), b);
-    unpack_bf16x8(__ldg(bp + 1), b + 8);
+__device__ __forceinline__ long long res_row(const DevEpi& ep, int m) {
+  return ep.res_row_mod > 0 ? (long long)(m % ep.res_row_mod) : (long long)m;
+}
+
+// Residual (bf16) and bias values of one 32-column chunk, fetched ahead of use.
+struct Chunk32 {
+  uint4 r[4];
+  uint4 b[4];
+};
+
+// N is a multiple of 16, so a chunk is either 32 columns wide or the 16-column
+// tail of the row; nothing at or beyond column N is read or written.
+__device__ __forceinline__ int chunk_vecs(const DevEpi& ep, int n) { return (n + 32 <= ep.N) ? 4 : 2; }
+
+__device__ __forceinline__ void prefetch32(const DevEpi& ep, int m, int n, bool row_ok, Chunk32& c) {
+  const int nv = chunk_vecs(ep, n);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] += b[i];
+  for (int i = 0; i < 4; ++i) c.r[i] = c.b[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (ep.residual != nullptr && row_ok) {
+    const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < nv) c.r[i] = rp[i];
+  }
+  if (ep.bias != nullptr) {
+    const uint4* bp = reinterpret_cast<const uint4*>(ep.bias + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < nv) c.b[i] = __ldg(bp + i);
+  }
+}
+
+// Finish the chunk [n, n+32) (or its 16-column tail) of row m held in v[] (fp32, alpha applied).
+__device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long long orow, float* v, bool row_ok,
+                                         const Chunk32& c) {
+  if (ep.bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float b[8];
+      unpack_bf16x8(c.b[i], b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[8 * i + e] += b[e];
+    }
   }
   if (ep.act == VLA_ACT_GELU_TANH) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = gelu_tanh_f(v[i]);
+    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
   }
   if (!row_ok) return;
+  const int nv = chunk_vecs(ep, n);
   if (ep.act == VLA_ACT_EULER) {
     float* xp = ep.euler_x + (long long)m * ep.ldx + n;
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) {
+    for (int i = 0; i < 32; i += 4) {
+      if (i >= 8 * nv) break;
       float4 x = *reinterpret_cast<float4*>(xp + i);
       x.x += ep.euler_dt * v[i];
       x.y += ep.euler_dt * v[i + 1];
@@ -106,17 +142,83 @@ __device__ __forceinline__ void finish16(const DevEpi& ep, int m, int n, long lo
     }
   }
   if (ep.residual != nullptr) {
-    const long long rr = ep.res_row_mod > 0 ? (long long)(m % ep.res_row_mod) : (long long)m;
-    const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + rr * ep.ldr + n);
-    float r[16];
-    unpack_bf16x8(rp[0], r);
-    unpack_bf16x8(rp[1], r + 8);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] += r[i];
+    for (int i = 0; i < 4; ++i) {
+      float r[8];
+      unpack_bf16x8(c.r[i], r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[8 * i + e] += r[e];
+    }
   }
   uint4* cp = reinterpret_cast<uint4*>(ep.C + orow * ep.ldc + n);
-  cp[0] = pack_bf16x8(v);
-  cp[1] = pack_bf16x8(v + 8);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (i < nv) cp[i] = pack_bf16x8(v + 8 * i);
+}
+
+// RoPE on one 64-wide head [n, n+64) of row m: rotate pairs (d, d+32), d < 32,
+// in two 16-pair halves (cos / sin read as float4 from the [pos][64] table).
+__device__ __forceinline__ void rope_head(const DevEpi& ep, uint32_t taddr, int m, int n, long long orow,
+                                          bool row_ok) {
+  const bool rot = n < ep.rope_ncols;
+  const float* cs = ep.rope_cs + (long long)(m % ep.rope_seq) * 64;
+#pragma unroll
+  for (int hq = 0; hq < 2; ++hq) {
+    float lo[16], hi[16];
+    tmem_ld16(taddr + 16 * hq, lo);
+    tmem_ld16(taddr + 32 + 16 * hq, hi);
+    if (!row_ok) continue;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      lo[i] *= ep.alpha;
+      hi[i] *= ep.alpha;
+    }
+    if (ep.bias != nullptr) {
+      float b[8];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 16 * hq) + i), b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lo[8 * i + e] += b[e];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 32 + 16 * hq) + i), b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hi[8 * i + e] += b[e];
+      }
+    }
+    if (rot) {
+      const float4* c4 = reinterpret_cast<const float4*>(cs + 16 * hq);
+      const float4* s4 = reinterpret_cast<const float4*>(cs + 32 + 16 * hq);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 c = __ldg(c4 + i), sn = __ldg(s4 + i);
+        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = lo[4 * i + e], b = hi[4 * i + e];
+          lo[4 * i + e] = a * cc[e] - b * ss[e];
+          hi[4 * i + e] = b * cc[e] + a * ss[e];
+        }
+      }
+    }
+    if (ep.residual != nullptr) {
+      const bf16* rp = ep.residual + res_row(ep, m) * ep.ldr + n;
+      float r[8];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 16 * hq)[i], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lo[8 * i + e] += r[e];
+        unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 32 + 16 * hq)[i], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hi[8 * i + e] += r[e];
+      }
+    }
+    bf16* cp = ep.C + orow * ep.ldc + n;
+    reinterpret_cast<uint4*>(cp + 16 * hq)[0] = pack_bf16x8(lo);
+    reinterpret_cast<uint4*>(cp + 16 * hq)[1] = pack_bf16x8(lo + 8);
+    reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[0] = pack_bf16x8(hi);
+    reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[1] = pack_bf16x8(hi + 8);
+  }
 }
 
 // Epilogue of one 128 x BN accumulator tile for one row m; warps that share a
@@ -129,47 +231,9 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
   if (ep.act == VLA_ACT_ROPE) {
 #pragma unroll 1
     for (int h = 64 * part; h < BN; h += 64 * nparts) {
-      float x[64];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) tmem_ld16(taddr + h + 16 * j, x + 16 * j);
       const int n = n0 + h;
-      if (n >= ep.N) continue;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) x[i] *= ep.alpha;
-      if (ep.bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float b[8];
-          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n) + j), b);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) x[8 * j + i] += b[i];
-        }
-      }
-      if (n < ep.rope_ncols && row_ok) {
-        const float* cs = ep.rope_cs + (long long)(m % ep.rope_seq) * 64;
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-          const float c = __ldg(cs + d), s = __ldg(cs + 32 + d);
-          const float a = x[d], b = x[d + 32];
-          x[d] = a * c - b * s;
-          x[d + 32] = b * c + a * s;
-        }
-      }
-      if (!row_ok) continue;
-      if (ep.residual != nullptr) {
-        const long long rr = ep.res_row_mod > 0 ? (long long)(m % ep.res_row_mod) : (long long)m;
-        const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + rr * ep.ldr + n);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float r[8];
-          unpack_bf16x8(rp[j], r);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) x[8 * j + i] += r[i];
-        }
-      }
-      uint4* cp = reinterpret_cast<uint4*>(ep.C + orow * ep.ldc + n);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cp[j] = pack_bf16x8(x + 8 * j);
+      if (n >= ep.N) break;
+      rope_head(ep, taddr + h, m, n, orow, row_ok);
     }
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
@@ -183,8 +247,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * ep.alpha) * (u[i] * ep.alpha);
       const int nc = n >> 1;
       if (ep.residual != nullptr) {
-        const long long rr = ep.res_row_mod > 0 ? (long long)(m % ep.res_row_mod) : (long long)m;
-        const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + rr * ep.ldr + nc);
+        const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + nc);
         float r[16];
         unpack_bf16x8(rp[0], r);
         unpack_bf16x8(rp[1], r + 8);
@@ -196,22 +259,28 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       cp[1] = pack_bf16x8(g + 8);
     }
   } else {
+    // 32-column chunks; the next chunk's residual / bias loads are issued before
+    // this chunk's stores so their latency overlaps (C may alias the residual).
+    const int step = 32 * nparts;
+    int c = 32 * part;
+    Chunk32 cur, nxt;
+    if (c < BN && n0 + c < ep.N) prefetch32(ep, m, n0 + c, row_ok, cur);
 #pragma unroll 1
-    for (int c = 32 * part; c < BN; c += 32 * nparts) {
+    for (; c < BN; c += step) {
+      const int n = n0 + c;
+      if (n >= ep.N) break;
+      float v[32];
+      tmem_ld16(taddr + c, v);
+      tmem_ld16(taddr + c + 16, v + 16);
+      const bool more = c + step < BN && n + step < ep.N;
+      if (more) prefetch32(ep, m, n + step, row_ok, nxt);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float v[16];
-        tmem_ld16(taddr + c + 16 * half, v);
-        const int n = n0 + c + 16 * half;
-        if (n >= ep.N) continue;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= ep.alpha;
-        finish16(ep, m, n, orow, v, row_ok);
-      }
+      for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
+      finish32(ep, m, n, orow, v, row_ok, cur);
+      if (more) cur = nxt;
     }
   }
 }
-
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)

@@ -11,7 +11,7 @@ namespace gemm {
 // SMs, each tile costing (BN + 48) column-units (48 ~ fixed A-tile and
 // epilogue overhead per tile).
 static int choose_bn(int64_t M, int64_t N, int act, int num_sms) {
-  const int cands[4] = {256, 128, 64, 32};
+  const int cands[8] = {256, 224, 192, 160, 128, 96, 64, 32};
   int best = 0;
   double best_cost = 1e300;
   for (int bn : cands) {
@@ -52,7 +52,7 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const De
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
     if (ep.residual) bytes += 2.0 * M * out_cols;
     if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
-    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes);
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K);
   }
   return launch_status("gemm_bf16_tc");
 }
@@ -121,7 +121,11 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, ep, M, N, K, st);
+    case 224: return launch_bn<224>(ta, B, ldb, ep, M, N, K, st);
+    case 192: return launch_bn<192>(ta, B, ldb, ep, M, N, K, st);
+    case 160: return launch_bn<160>(ta, B, ldb, ep, M, N, K, st);
     case 128: return launch_bn<128>(ta, B, ldb, ep, M, N, K, st);
+    case 96: return launch_bn<96>(ta, B, ldb, ep, M, N, K, st);
     case 64: return launch_bn<64>(ta, B, ldb, ep, M, N, K, st);
     case 32: return launch_bn<32>(ta, B, ldb, ep, M, N, K, st);
     default: return set_error(VLA_E_UNSUPPORTED, "gemm: tile width %d not built", bn);

@@ -111,6 +111,7 @@ struct ProfRec {
   int kind;
   double flops, bytes;
   cudaEvent_t a, b;
+  int64_t m, n, k;
 };
 struct Profiler {
   bool on = false;
@@ -126,11 +127,12 @@ static inline void prof_begin(cudaStream_t st) {
   g_prof.pending = g_prof.pool[g_prof.next++];
   cudaEventRecord(g_prof.pending, st);
 }
-static inline void prof_end(cudaStream_t st, int kind, double flops, double bytes) {
+static inline void prof_end(cudaStream_t st, int kind, double flops, double bytes, int64_t m = 0, int64_t n = 0,
+                            int64_t k = 0) {
   if (!g_prof.on || g_prof.pending == nullptr || g_prof.next + 1 > g_prof.pool.size()) return;
   cudaEvent_t e = g_prof.pool[g_prof.next++];
   cudaEventRecord(e, st);
-  g_prof.recs.push_back(ProfRec{kind, flops, bytes, g_prof.pending, e});
+  g_prof.recs.push_back(ProfRec{kind, flops, bytes, g_prof.pending, e, m, n, k});
   g_prof.pending = nullptr;
 }
 

@@ -92,6 +92,9 @@ int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count) 
       out[n].ms = ms;
       out[n].flops = r.flops;
       out[n].bytes = r.bytes;
+      out[n].m = r.m;
+      out[n].n = r.n;
+      out[n].k = r.k;
     }
     ++n;
   }
@@ -116,7 +119,7 @@ int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
 
 int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
                         int64_t N, int64_t K, const vla_epilogue* epi, int tile_n, vla_stream_t stream) {
-  VLA_CHECK_ARG(tile_n == 32 || tile_n == 64 || tile_n == 128 || tile_n == 256, "tile_n must be 32/64/128/256");
+  VLA_CHECK_ARG(tile_n >= 32 && tile_n <= 256 && tile_n % 32 == 0, "tile_n must be a multiple of 32 in [32, 256]");
   return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n);
 }
 
@@ -207,7 +210,8 @@ int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream) {
   p.causal = a->causal;
   p.kv_len = a->kv_len;
   p.scale_log2 = a->scale * 1.4426950408889634f;
-  return blocks::attention(p, a->batch, as_stream(stream));
+  VLA_CHECK_ARG(a->impl >= VLA_ATTN_AUTO && a->impl <= VLA_ATTN_TCGEN05, "attention: unknown impl %d", a->impl);
+  return blocks::attention(p, a->batch, as_stream(stream), a->impl);
 }
 
 int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, int32_t scale, int32_t C,

@@ -67,8 +67,13 @@ class AttentionArgs(ctypes.Structure):
         ("o_batch", ctypes.c_int64),
         ("batch", ctypes.c_int32), ("Lq", ctypes.c_int32), ("Lk", ctypes.c_int32), ("Hq", ctypes.c_int32),
         ("Hkv", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("causal", ctypes.c_int32),
-        ("kv_len", ctypes.c_void_p), ("scale", ctypes.c_float),
+        ("kv_len", ctypes.c_void_p), ("scale", ctypes.c_float), ("impl", ctypes.c_int32),
     ]
+
+
+ATTN_AUTO = 0
+ATTN_MMA_SYNC = 1
+ATTN_TCGEN05 = 2
 
 
 class LlamaLayer(ctypes.Structure):
@@ -99,7 +104,7 @@ class ProfileRecord(ctypes.Structure):
     """Mirror of ``vla_profile_record``."""
 
     _fields_ = [("kind", ctypes.c_int32), ("ms", ctypes.c_float), ("flops", ctypes.c_double),
-                ("bytes", ctypes.c_double)]
+                ("bytes", ctypes.c_double), ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64)]
 
 
 KIND_NAMES = ["gemm", "attention", "norm", "rope", "softmax", "elementwise", "layout"]

@@ -115,7 +115,7 @@ def elementwise(op: int, x: torch.Tensor, y: Optional[torch.Tensor] = None,
 
 
 def attention(q, k, v, o, *, batch, Lq, Lk, Hq, Hkv, q_batch, k_batch, v_batch, o_batch, causal=False,
-              kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+              kv_len: Optional[torch.Tensor] = None, impl: int = 0) -> torch.Tensor:
     """Flash attention over `batch` sequences; q/k/v/o are 2-D row views whose row
     strides are their stride(0); sequence b starts ``*_batch`` elements later."""
     a = _lib.AttentionArgs()
@@ -126,6 +126,7 @@ def attention(q, k, v, o, *, batch, Lq, Lk, Hq, Hkv, q_batch, k_batch, v_batch, 
     a.causal = 1 if causal else 0
     a.kv_len = None if kv_len is None else kv_len.data_ptr()
     a.scale = 0.125
+    a.impl = impl
     _lib.call("vla_attention_bf16", ctypes.byref(a), _stream())
     return o
 
