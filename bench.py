@@ -456,22 +456,29 @@ def run_ours(args, rank, world, local):
                 gbs = a["bytes"] / (a["ms"] * 1e-3) / 1e9
                 ent.update(achieved_gbs=round(gbs, 1), frac_of_hbm=round(gbs / hbm_peak, 3))
             kernels[k] = ent
-        g = agg.get("gemm")
+        # dominant single kernel: the GEMM shape with the largest share of the step
+        top = extras["gemm_shapes"][0] if extras.get("gemm_shapes") else None
         traffic = None
         try:
-            prof = json.load(open(os.path.join(ROOT, "profiles", "gemm_traffic.json")))
-            traffic = prof.get("dram_bytes_per_launch")
-        except (OSError, ValueError):
+            import re
+            txt = open(os.path.join(ROOT, "profiles", "gemm_fc1_siglip.md")).read()
+            mt = re.search(r"dram_bytes_per_launch: (\d+) \(M=(\d+)\)", txt)
+            if mt and top and top["mnk"][1:] == [3072, 768]:
+                # ncu capture of the same GEMM at fewer rows; DRAM traffic grows with M
+                traffic = int(mt.group(1)) * top["mnk"][0] / int(mt.group(2))
+        except OSError:
             pass
-        if g:
-            ach = g["flops"] / (g["ms"] * 1e-3) / 1e12
-            roofline = {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel (all GEMM launches of one step)",
+        if top:
+            ach = 2.0 * top["mnk"][0] * top["mnk"][1] * top["mnk"][2] * top["launches"] / (top["ms"] * 1e-3) / 1e12
+            roofline = {"bound": "tensor",
+                        "kernel": f"gemm_bf16_tc_kernel M,N,K={top['mnk']} ({top['launches']} launches per step)",
                         "achieved": round(ach, 1), "peak": tflops_peak, "unit": "TFLOP/s",
                         "frac": round(ach / tflops_peak, 4), "traffic": traffic,
+                        "traffic_note": "ncu dram read+write per launch, scaled by rows from the M=16384 capture "
+                                        "(profiles/gemm_fc1_siglip.md)",
                         "peak_source": f"{peak_src} bf16_tflops_sustained",
-                        "launches_per_step": g["launches"],
-                        "algorithmic_flops_per_launch": g["flops"] / g["launches"],
-                        "avg_launch_ms": g["ms"] / g["launches"]}
+                        "algorithmic_flops_per_launch": 2.0 * top["mnk"][0] * top["mnk"][1] * top["mnk"][2],
+                        "avg_launch_ms": top["ms"] / top["launches"]}
         if not args.no_extras and world == 1:
             try:
                 extras["blocks"] = block_timings(torch)

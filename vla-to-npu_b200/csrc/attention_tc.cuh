@@ -287,38 +287,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           float s[BKV];
 #pragma unroll
           for (int c = 0; c < BKV; c += 32) tmem_ld32(sadr + c, s + c);
-          float mx = -INFINITY;
-          if (key0 + BKV <= Lk) {
+          // row max over raw scores with 8 independent accumulators (short dependency chains)
+          if (key0 + BKV > Lk) {
 #pragma unroll
-            for (int c = 0; c < BKV; ++c) {
-              s[c] *= p.scale_log2;
-              mx = fmaxf(mx, s[c]);
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < BKV; ++c) {
-              s[c] = (key0 + c < Lk) ? s[c] * p.scale_log2 : -INFINITY;
-              mx = fmaxf(mx, s[c]);
-            }
+            for (int c = 0; c < BKV; ++c)
+              if (key0 + c >= Lk) s[c] = -INFINITY;
           }
-          const float mnew = fmaxf(m, mx);
+          float mx8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+          for (int c = 8; c < BKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+#pragma unroll
+          for (int i = 1; i < 8; ++i) mx8[0] = fmaxf(mx8[0], mx8[i]);
+          const float mnew = fmaxf(m, mx8[0] * p.scale_log2);
           const float mbase = mnew == -INFINITY ? 0.f : mnew;
           alpha = ex2_fast(m - mbase);
           m = mnew;
-          float rs = 0.f;
-          // P row (128 keys, bf16) into the two swizzled 64-key atoms of P buffer tt%2
+          float rs8[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+          // P row (128 keys, bf16) into the two swizzled 64-key atoms of P buffer tt%2;
+          // exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2
           uint8_t* prow = sm.p[tt & 1] + row * 128;
 #pragma unroll
           for (int c8 = 0; c8 < BKV / 8; ++c8) {
             float e[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              e[i] = ex2_fast(s[c8 * 8 + i] - mbase);
-              rs += e[i];
+              e[i] = ex2_fast(fmaf(s[c8 * 8 + i], p.scale_log2, -mbase));
+              rs8[i] += e[i];
             }
             const int atom = c8 >> 3, chunk = c8 & 7;
             *reinterpret_cast<uint4*>(prow + atom * 16384 + ((chunk ^ (row & 7)) << 4)) = pack_bf16x8(e);
           }
+          float rs = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rs += rs8[i];
           l = l * alpha + rs;
           // make the generic-proxy smem writes of P visible to the tensor core
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
