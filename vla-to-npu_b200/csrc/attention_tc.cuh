@@ -7,11 +7,12 @@
 //              S = Q K^T completes, V after P.V)
 //   warp 1     TMEM allocator + single-thread MMA issuer:
 //                S_j  = Q . K_j^T   (UMMA 128x128x16, A = Q, B = K, both K-major)
-//                PV_j = P_j . V_j   (UMMA 128x64x16, A = P from smem K-major,
+//                PV_j = P_j . V_j   (UMMA 128x64x16, A = P from tensor memory,
 //                                    B = V from smem MN-major, no transpose pass)
 //   warps 2..5 softmax: thread r owns query row r; reads its S row from TMEM
 //              (so row max / sum need no shuffles), P = exp2(S*scale*log2e - m)
-//              rounded to bf16 into swizzled smem for the P.V MMA, and keeps the
+//              rounded to bf16 and stored back into the S columns of TMEM (no
+//              shared-memory round trip) for the P.V MMA, and keeps the
 //              output row O (64 fp32) in registers: O = O*alpha + PV.
 // S is double-buffered in TMEM (S_{j+1} is computed while row j is in softmax),
 // P and PV are double-buffered too.  TMEM: 2 x 128 (S) + 2 x 64 (PV) columns.
@@ -31,7 +32,6 @@ constexpr int kKStages = 3;
 constexpr int kVStages = 3;
 constexpr int kThreads = 192;
 constexpr int TILE_BYTES = BKV * HD * 2;  // 16 KB: a [128 x 64] bf16 tile (Q, K or V)
-constexpr int P_BYTES = BQ * BKV * 2;     // 32 KB: P as two [128 x 64] swizzled atoms
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL0 = 0;     // S buffers at columns 0 and 128
 constexpr uint32_t PV_COL0 = 256;  // PV buffers at columns 256 and 320
@@ -50,7 +50,6 @@ struct Smem {
   uint8_t q[2][TILE_BYTES];
   uint8_t k[kKStages][TILE_BYTES];
   uint8_t v[kVStages][TILE_BYTES];
-  uint8_t p[2][P_BYTES];
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
@@ -65,20 +64,35 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
+// 32 lanes x 64 consecutive 32-bit TMEM columns from registers, then wait.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t* r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, "
+      "%33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, "
+      "%49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]),
+      "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]),
+      "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]),
+      "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x K) read from tensor memory with
+// two bf16 K-elements per 32-bit column (element 2c in the low half).
+__device__ __forceinline__ void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // MN-major SW128 descriptor for a [rows x 64] bf16 tile read along the row
@@ -235,15 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ok) ok = mbar_wait_bounded(&sm.v_full[sv], (tp / kVStages) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t pbase = smem_u32(sm.p[tp & 1]);
+            // P (bf16, packed in pairs) lives in the first 64 columns of S buffer tp%2
+            const uint32_t pt = tmem + S_COL0 + (uint32_t)(tp & 1) * BKV;
             const uint32_t vbase = smem_u32(sm.v[sv]);
             const uint32_t d = tmem + PV_COL0 + (uint32_t)(tp & 1) * HD;
 #pragma unroll
             for (int k = 0; k < BKV / 16; ++k) {
-              const uint64_t adesc =
-                  make_sw128_desc(pbase + (uint32_t)(k >> 2) * 16384u + (uint32_t)(k & 3) * 32u);
               const uint64_t bdesc = make_sw128_mn_desc(vbase + (uint32_t)k * 2048u);
-              tc_mma_bf16(d, adesc, bdesc, idesc_pv, k > 0);
+              tc_mma_bf16_ts(d, pt + (uint32_t)k * 8u, bdesc, idesc_pv, k > 0);
             }
             tc_commit(&sm.pv_full[tp & 1]);
             tc_commit(&sm.v_empty[sv]);
@@ -285,8 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sadr = tmem + lane_base + S_COL0 + (uint32_t)(tt & 1) * BKV;
           const int key0 = j * BKV;
           float s[BKV];
-#pragma unroll
-          for (int c = 0; c < BKV; c += 32) tmem_ld32(sadr + c, s + c);
+          tmem_ld128(sadr, s);
           // row max over raw scores with 8 independent accumulators (short dependency chains)
           if (key0 + BKV > Lk) {
 #pragma unroll
@@ -307,26 +319,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           float rs8[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
-          // P row (128 keys, bf16) into the two swizzled 64-key atoms of P buffer tt%2;
-          // exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2
-          uint8_t* prow = sm.p[tt & 1] + row * 128;
+          // P row (128 keys): exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2, packed
+          // as 64 bf16 pairs into the first 64 TMEM columns of this S buffer (the
+          // scores are already in registers); the P.V MMA reads it from there
+          uint32_t pk[BKV / 2];
 #pragma unroll
-          for (int c8 = 0; c8 < BKV / 8; ++c8) {
-            float e[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              e[i] = ex2_fast(fmaf(s[c8 * 8 + i], p.scale_log2, -mbase));
-              rs8[i] += e[i];
-            }
-            const int atom = c8 >> 3, chunk = c8 & 7;
-            *reinterpret_cast<uint4*>(prow + atom * 16384 + ((chunk ^ (row & 7)) << 4)) = pack_bf16x8(e);
+          for (int c = 0; c < BKV; c += 2) {
+            const float e0 = ex2_fast(fmaf(s[c], p.scale_log2, -mbase));
+            const float e1 = ex2_fast(fmaf(s[c + 1], p.scale_log2, -mbase));
+            rs8[c & 7] += e0;
+            rs8[(c + 1) & 7] += e1;
+            pk[c >> 1] = pack_bf16x2(e0, e1);
           }
+          tmem_st64(sadr, pk);
           float rs = 0.f;
 #pragma unroll
           for (int i = 0; i < 8; ++i) rs += rs8[i];
           l = l * alpha + rs;
-          // make the generic-proxy smem writes of P visible to the tensor core
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           tc_fence_before();
           mbar_arrive(&sm.p_full[tt & 1]);
         }
@@ -338,8 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t padr = tmem + lane_base + PV_COL0 + (uint32_t)(tp & 1) * HD;
           float pv[HD];
-          tmem_ld32(padr, pv);
-          tmem_ld32(padr + 32, pv + 32);
+          tmem_ld64(padr, pv);
           tc_fence_before();
           mbar_arrive(&sm.pv_empty[tp & 1]);
 #pragma unroll
