@@ -96,6 +96,12 @@ int vla_abi_sizes(int64_t* out, int32_t n);
  * devices, all threads); a graph replay re-runs captured launches without
  * counting them again. */
 uint64_t vla_launch_count(void);
+/* Launch overlap between consecutive kernels of this library on one stream
+ * (programmatic dependent launch: a kernel may be scheduled while its
+ * predecessor drains and waits for the predecessor's results before its first
+ * global-memory access).  On by default; 0 disables it.  Returns the previous
+ * setting.  No counterpart in the reference (its NPU calls are synchronous). */
+int vla_set_launch_overlap(int32_t enable);
 
 /* Launch profiler (measurement only; no counterpart in the reference, whose
  * timing is the XRT host's "NPU execution time" print, gemm/v1_test_tiled_gemm.py:81-96).

@@ -127,3 +127,44 @@ def test_vision_tower_c2(cuda):
     ref32 = R.vision_tower(obs["images"], params, cfg, dt=F32)
     refbf = R.vision_tower(obs["images"], params, cfg, dt=BF)
     check(ours, ref32, refbf, "vision tower + connector C2", gate_tol=2e-1)
+
+
+def test_infer_host_stream_matches_per_batch(cuda):
+    """The overlapped host API (copies of batch k+1 during compute of batch k,
+    double-buffered staging) gives exactly the per-batch results."""
+    from vla_b200.model import SmolVLA
+    cfg = tiny_cfg()
+    params = W.smolvla_params(cfg, seed=0)
+    m = SmolVLA(cfg, params, "cuda")
+    batches, refs = [], []
+    for s in range(3):
+        obs = W.observation_batch(cfg, 2, seed=10 + s)
+        host = tuple(obs[k].pin_memory() for k in ("images", "token_ids", "state", "noise"))
+        batches.append(host)
+        refs.append(m.infer(*(t.cuda() for t in host)).clone().cpu())
+    outs = [torch.empty(2, cfg.expert.chunk, cfg.expert.action_dim).pin_memory() for _ in range(3)]
+    m.infer_host_stream(batches, outs)
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+
+
+def test_launch_overlap_is_bit_exact(cuda):
+    """Programmatic dependent launch changes only scheduling: the whole pipeline
+    (eager and CUDA-graph) gives identical bits with the overlap on and off."""
+    from vla_b200 import _lib
+    from vla_b200.model import SmolVLA
+    cfg = tiny_cfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, 3, seed=5)
+    args = [obs[k].cuda() for k in ("images", "token_ids", "state", "noise")]
+    lib = _lib.load()
+    outs = {}
+    try:
+        for ov in (0, 1):
+            lib.vla_set_launch_overlap(ov)
+            m = SmolVLA(cfg, params, "cuda")
+            outs[ov] = (m.infer(*args, use_graph=False).clone(), m.infer(*args, use_graph=True).clone())
+    finally:
+        lib.vla_set_launch_overlap(1)
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(outs[1][0], outs[1][1])

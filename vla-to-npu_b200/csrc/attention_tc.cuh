@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  pdl_prologue();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------

@@ -32,10 +32,10 @@ static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const vo
   const int grid = (int)((M + norm::kWarps - 1) / norm::kWarps);
   prof_begin(st);
   if (mode == 0)
-    norm::rownorm_kernel<0><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, nullptr,
+    launch_k(norm::rownorm_kernel<0>, dim3(grid), dim3(norm::kWarps * 32), 0, st, (const bf16*)x, ldx, (const bf16*)g, nullptr,
                                                                  (bf16*)y, ldy, (int)M, (int)N, eps);
   else
-    norm::rownorm_kernel<1><<<grid, norm::kWarps * 32, 0, st>>>((const bf16*)x, ldx, (const bf16*)g, (const bf16*)b,
+    launch_k(norm::rownorm_kernel<1>, dim3(grid), dim3(norm::kWarps * 32), 0, st, (const bf16*)x, ldx, (const bf16*)g, (const bf16*)b,
                                                                  (bf16*)y, ldy, (int)M, (int)N, eps);
   prof_end(st, VLA_KIND_NORM, 0.0, 4.0 * (double)M * N);
   return launch_status("rownorm");
@@ -87,7 +87,7 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
   const int sms = device_info().num_sms;
   const int grid = (int)(items < sms ? items : sms);
   prof_begin(st);
-  attn_tc::flash_attn_tc_kernel<<<grid, attn_tc::kThreads, smem, st>>>(tq, tk, tv, tp);
+  launch_k(attn_tc::flash_attn_tc_kernel, dim3(grid), dim3(attn_tc::kThreads), smem, st, tq, tk, tv, tp);
   prof_end(st, VLA_KIND_ATTENTION, 4.0 * batch * p.Hq * (double)p.Lq * p.Lk * 64,
            2.0 * batch * ((double)p.Lq * p.Hq * 64 * 2 + (double)p.Lk * p.Hkv * 64 * 2));
   return launch_status("flash_attn_tc");
@@ -109,7 +109,7 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl
     return attention_tc(p, batch, st);
   dim3 grid((p.Lq + attn::BQ - 1) / attn::BQ, p.Hq, batch);
   prof_begin(st);
-  attn::flash_attn_kernel<<<grid, attn::kThreads, 0, st>>>(p);
+  launch_k(attn::flash_attn_kernel, dim3(grid), dim3(attn::kThreads), 0, st, p);
   {
     const double lk = (double)p.Lk;
     const double flops = 4.0 * batch * p.Hq * (double)p.Lq * lk * attn::HD;

@@ -228,6 +228,17 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
 }
 
 // --------------------------------------------------------------------------
+// Programmatic dependent launch: let the next kernel in the stream launch as
+// soon as every block of this one has started (its prologue then overlaps our
+// tail), and wait for the previous kernel's results before touching global
+// memory.  Both are no-ops when the launch did not enable the overlap.
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_prologue() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// --------------------------------------------------------------------------
 // small math helpers
 // --------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {

@@ -16,6 +16,7 @@ namespace ew {
 // ---------------------------------------------------------------------------
 __global__ void rope_kernel(bf16* __restrict__ x, long long ld, long long M, int ncols, int seq,
                             const float* __restrict__ cs) {
+  pdl_prologue();
   // one thread per (row, head, 8-pair group): handles d in [8j, 8j+8) and d+32
   const int groups_per_row = (ncols / 64) * 4;
   const long long total = M * groups_per_row;
@@ -50,6 +51,7 @@ __global__ void rope_kernel(bf16* __restrict__ x, long long ld, long long M, int
 // ---------------------------------------------------------------------------
 __global__ void softmax_kernel(const bf16* __restrict__ x, long long ldx, bf16* __restrict__ y, long long ldy, int M,
                                int N, float scale, int causal_row_start) {
+  pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= M) return;
@@ -78,6 +80,7 @@ __global__ void softmax_kernel(const bf16* __restrict__ x, long long ldx, bf16* 
 // ---------------------------------------------------------------------------
 __global__ void act_kernel(const bf16* __restrict__ x, long long ldx, const bf16* __restrict__ y2, long long ldy2,
                            bf16* __restrict__ out, long long ldo, long long M, int N, int op) {
+  pdl_prologue();
   const int vpr = N >> 3;
   const long long total = M * vpr;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -107,6 +110,7 @@ __global__ void act_kernel(const bf16* __restrict__ x, long long ldx, const bf16
 // ---------------------------------------------------------------------------
 __global__ void pixel_shuffle_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int B, int grid, int s,
                                      int C) {
+  pdl_prologue();
   const int cv = C >> 3;
   const long long total = (long long)B * grid * grid * cv;
   const int g2 = grid / s;
@@ -134,6 +138,7 @@ __global__ void pixel_shuffle_kernel(const bf16* __restrict__ in, bf16* __restri
 // ---------------------------------------------------------------------------
 __global__ void im2col_kernel(const bf16* __restrict__ img, bf16* __restrict__ out, int B, int Cin, int H, int W,
                               int p) {
+  pdl_prologue();
   const int gh = H / p, gw = W / p;
   const int kdim = Cin * p * p;
   const int vec_per_row = kdim >> 3;
@@ -160,6 +165,7 @@ __global__ void im2col_kernel(const bf16* __restrict__ img, bf16* __restrict__ o
 __global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict__ table, int vocab, int H, int B,
                              int T, float scale, bf16* __restrict__ out, long long ldo, int rows_per_seq,
                              int row_offset) {
+  pdl_prologue();
   const int hv = H >> 3;
   const long long total = (long long)B * T * hv;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -181,6 +187,7 @@ __global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict
 // fp32 -> bf16 copy of a [M, N] matrix (row strides in elements)
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, long long ldx, bf16* __restrict__ y, long long ldy,
                                    long long M, int N) {
+  pdl_prologue();
   const long long total = M * N;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {

@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_prologue();
 
   if (warp == 0) {
     if (lane == 0) {

@@ -46,7 +46,7 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const De
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
   prof_begin(st);
-  gemm_bf16_tc_kernel<BN><<<grid, kThreads, Cf::SMEM_BYTES, st>>>(ta, tb, ep, (int)M, (int)N, (int)K);
+  launch_k(gemm_bf16_tc_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ep, (int)M, (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -95,6 +96,25 @@ static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, ui
                      (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld, box_inner,
                      box_outer);
   return VLA_OK;
+}
+
+// Launch overlap (programmatic dependent launch) for every kernel of this
+// library; on by default, switchable with vla_set_launch_overlap().
+static std::atomic<int> g_launch_overlap{1};
+
+template <typename... KArgs, typename... Args>
+static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_launch_overlap.load(std::memory_order_relaxed) ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 static inline cudaStream_t as_stream(vla_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }

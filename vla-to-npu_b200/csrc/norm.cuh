@@ -23,6 +23,7 @@ __global__ void __launch_bounds__(kWarps * 32) rownorm_kernel(const bf16* __rest
                                                               const bf16* __restrict__ g, const bf16* __restrict__ b,
                                                               bf16* __restrict__ y, long long ldy, int M, int N,
                                                               float eps) {
+  pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kWarps + warp;
   if (row >= M) return;

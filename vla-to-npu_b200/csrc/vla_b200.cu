@@ -65,6 +65,11 @@ int vla_peek_device_error(unsigned int* code) {
 
 uint64_t vla_launch_count(void) { return g_launch_count.load(); }
 
+int vla_set_launch_overlap(int32_t enable) {
+  const int old = g_launch_overlap.exchange(enable ? 1 : 0);
+  return old;
+}
+
 int vla_profile_start(int32_t capacity) {
   VLA_CHECK_ARG(capacity > 0, "profile_start: capacity must be positive");
   VLA_CHECK_ARG(!g_prof.on, "profile_start: profiler already running");
@@ -139,7 +144,7 @@ int vla_rope_bf16(void* x, int64_t ld, int64_t M, int32_t ncols, int32_t seq, co
   if (M == 0) return VLA_OK;
   const long long work = M * (ncols / 64) * 4;
   prof_begin(as_stream(stream));
-  ew::rope_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((bf16*)x, ld, M, ncols, seq, cs);
+  launch_k(ew::rope_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (bf16*)x, ld, M, ncols, seq, cs);
   prof_end(as_stream(stream), VLA_KIND_ROPE, 0.0, 4.0 * (double)M * ncols);
   return launch_status("rope");
 }
@@ -165,7 +170,7 @@ int vla_softmax_bf16(const void* x, int64_t ldx, void* y, int64_t ldy, int64_t M
   if (M == 0) return VLA_OK;
   const int wpb = 8;
   prof_begin(as_stream(stream));
-  ew::softmax_kernel<<<(int)((M + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(
+  launch_k(ew::softmax_kernel, dim3((int)((M + wpb - 1) / wpb)), dim3(wpb * 32), 0, as_stream(stream), 
       (const bf16*)x, ldx, (bf16*)y, ldy, (int)M, (int)N, scale, causal_row_start);
   prof_end(as_stream(stream), VLA_KIND_SOFTMAX, 0.0, 4.0 * (double)M * N);
   return launch_status("softmax");
@@ -180,7 +185,7 @@ int vla_elementwise_bf16(int32_t op, const void* x, int64_t ldx, const void* y2,
                   "elementwise: alignment");
   if (M == 0) return VLA_OK;
   prof_begin(as_stream(stream));
-  ew::act_kernel<<<blocks::grid_for(M * (N / 8), 256), 256, 0, as_stream(stream)>>>(
+  launch_k(ew::act_kernel, dim3(blocks::grid_for(M * (N / 8), 256)), dim3(256), 0, as_stream(stream), 
       (const bf16*)x, ldx, (const bf16*)y2, ldy2, (bf16*)out, ldo, M, (int)N, op);
   prof_end(as_stream(stream), VLA_KIND_ELEMENTWISE, 0.0, (op >= 2 ? 6.0 : 4.0) * (double)M * N);
   return launch_status("elementwise");
@@ -222,7 +227,7 @@ int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, i
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * grid * grid * (C / 8);
   prof_begin(as_stream(stream));
-  ew::pixel_shuffle_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)in, (bf16*)out,
+  launch_k(ew::pixel_shuffle_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)in, (bf16*)out,
                                                                                        B, grid, scale, C);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * grid * grid * C);
   return launch_status("pixel_shuffle");
@@ -236,7 +241,7 @@ int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, in
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * (H / p) * (W / p) * (Cin * p * p / 8);
   prof_begin(as_stream(stream));
-  ew::im2col_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>((const bf16*)img, (bf16*)out, B, Cin,
+  launch_k(ew::im2col_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)img, (bf16*)out, B, Cin,
                                                                                 H, W, p);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * Cin * H * W);
   return launch_status("im2col");
@@ -251,7 +256,7 @@ int vla_embed_bf16(const int32_t* ids, const void* table, int32_t vocab, int32_t
   if (B == 0 || T == 0) return VLA_OK;
   const long long work = (long long)B * T * (H / 8);
   prof_begin(as_stream(stream));
-  ew::embed_kernel<<<blocks::grid_for(work, 256), 256, 0, as_stream(stream)>>>(
+  launch_k(ew::embed_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), 
       ids, (const bf16*)table, vocab, H, B, T, scale, (bf16*)out, ldo, rows_per_seq, row_offset);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * T * H);
   return launch_status("embed");
@@ -261,7 +266,7 @@ int vla_f32_to_bf16(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t M
   VLA_CHECK_ARG(x && y && M >= 0 && N > 0 && ldx >= N && ldy >= N, "f32_to_bf16: bad arguments");
   if (M == 0) return VLA_OK;
   prof_begin(as_stream(stream));
-  ew::f32_to_bf16_kernel<<<blocks::grid_for(M * N, 256), 256, 0, as_stream(stream)>>>(x, ldx, (bf16*)y, ldy, M,
+  launch_k(ew::f32_to_bf16_kernel, dim3(blocks::grid_for(M * N, 256)), dim3(256), 0, as_stream(stream), x, ldx, (bf16*)y, ldy, M,
                                                                                       (int)N);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 6.0 * (double)M * N);
   return launch_status("f32_to_bf16");

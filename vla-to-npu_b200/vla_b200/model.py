@@ -302,6 +302,57 @@ class SmolVLA:
         torch.cuda.current_stream(self.device).synchronize()
         return out
 
+    def infer_host_stream(self, batches, outs) -> list:
+        """End-to-end inference over a sequence of host batches with the transfers
+        overlapped: batch k+1's observations are copied host->device on a copy
+        stream (into one of two device staging sets) while batch k computes, and
+        each batch's actions are copied device->host into ``outs[k]`` (pinned)
+        right after its chunk graph.  ``batches`` holds (images, token_ids, state,
+        noise) tuples of pinned host tensors of one batch size.  Returns ``outs``
+        after the last copy completed."""
+        n = len(batches)
+        if n == 0:
+            return outs
+        B = batches[0][0].shape[0]
+        self.allocate(B)
+        if self.graph is None or self.graph_batch != B:
+            self.capture()
+        if getattr(self, "_stage_batch", 0) != B:
+            self._stage = [[torch.empty_like(t) for t in (self.in_images, self.in_ids, self.in_state, self.in_noise)]
+                           for _ in range(2)]
+            self._stage_batch = B
+            self._copy_stream = torch.cuda.Stream(self.device)
+        comp = torch.cuda.current_stream(self.device)
+        cs = self._copy_stream
+        copied = [torch.cuda.Event() for _ in range(2)]
+        consumed = [torch.cuda.Event() for _ in range(2)]
+
+        def h2d(k):
+            st = self._stage[k & 1]
+            with torch.cuda.stream(cs):
+                if k >= 2:
+                    cs.wait_event(consumed[k & 1])
+                imgs, ids, state, noise = batches[k]
+                st[0].copy_(imgs, non_blocking=True)
+                st[1].copy_(ids, non_blocking=True)
+                st[2].copy_(state, non_blocking=True)
+                st[3].copy_(noise.reshape(st[3].shape), non_blocking=True)
+                copied[k & 1].record(cs)
+
+        h2d(0)
+        for k in range(n):
+            if k + 1 < n:
+                h2d(k + 1)
+            st = self._stage[k & 1]
+            comp.wait_event(copied[k & 1])
+            for dst, src in zip((self.in_images, self.in_ids, self.in_state, self.in_noise), st):
+                dst.copy_(src, non_blocking=True)
+            consumed[k & 1].record(comp)
+            self.graph.replay()
+            outs[k].view(-1, self.cfg.expert.action_dim).copy_(self.x_t, non_blocking=True)
+        comp.synchronize()
+        return outs
+
     def infer(self, images, token_ids, state, noise, use_graph: bool = True) -> torch.Tensor:
         """Action chunks [B, chunk, action_dim] (fp32) for a batch of observations."""
         self.load_inputs(images, token_ids, state, noise)
