@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--kernel-case", default="",
                     help="run one kernel of the step on a fixed small case (for ncu captures) and print its timing: "
                          + ", ".join(KERNEL_CASES))
+    ap.add_argument("--ctas", type=int, default=0, choices=[0, 1, 2],
+                    help="GEMM kernel cases: force one CTA (1) or a CTA pair (2) per tile; 0 = automatic")
     return ap.parse_args()
 
 
@@ -66,6 +68,10 @@ KERNEL_CASES = {
     "gemm_fc1": "SigLIP fc1 GEMM + bias + GELU, M=16384 N=3072 K=768",
     "gemm_qkv": "SigLIP QKV GEMM + bias, M=16384 N=2304 K=768",
     "gemm_fc2": "SigLIP fc2 GEMM + bias + residual, M=16384 N=768 K=3072",
+    "gemm_plain": "plain GEMM (no epilogue work) at the fc1 shape, M=16384 N=3072 K=768",
+    "gemm_plain_k3072": "plain GEMM, M=16384 N=3072 K=3072",
+    "gemm_exp_down": "action-expert down projection + residual, M=12800 N=720 K=2048",
+    "gemm_exp_o": "action-expert output projection + residual, M=12800 N=720 K=960",
     "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
     "layer_norm": "SigLIP LayerNorm, 16384 x 768",
 }
@@ -82,14 +88,18 @@ def run_kernel_case(args):
     bf = torch.bfloat16
     if name.startswith("gemm"):
         M, N, K = {"gemm_fc1": (16384, 3072, 768), "gemm_qkv": (16384, 2304, 768),
-                   "gemm_fc2": (16384, 768, 3072)}[name]
+                   "gemm_fc2": (16384, 768, 3072), "gemm_plain": (16384, 3072, 768),
+                   "gemm_plain_k3072": (16384, 3072, 3072), "gemm_exp_down": (12800, 720, 2048),
+                   "gemm_exp_o": (12800, 720, 960)}[name]
         a = W.randn((M, K), 0, "kc.a").cuda()
         w = W.randn((N, K), 0, "kc.w", std=0.02).cuda()
         b = W.randn((N,), 0, "kc.b", std=0.01).cuda()
         c = torch.empty(M, N, dtype=bf, device="cuda")
-        res = W.randn((M, N), 0, "kc.r").cuda() if name == "gemm_fc2" else None
-        epi = dev.make_epilogue(bias=b, residual=res, act=_lib.ACT_GELU_TANH if name == "gemm_fc1" else 0)
-        fn = lambda: dev.gemm(a, w, c, epi)  # noqa: E731
+        res = W.randn((M, N), 0, "kc.r").cuda() if name in ("gemm_fc2", "gemm_exp_down", "gemm_exp_o") else None
+        plain = name.startswith("gemm_plain") or name.startswith("gemm_exp")
+        epi = dev.make_epilogue(bias=None if plain else b, residual=res,
+                                act=_lib.ACT_GELU_TANH if name == "gemm_fc1" else 0)
+        fn = lambda: dev.gemm(a, w, c, epi, ctas=args.ctas)  # noqa: E731
         flops, nbytes = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * N * (2 if res is not None else 1))
     elif name == "attn_vision":
         B, L, H = 16, 1024, 12
@@ -309,13 +319,13 @@ def profile_pass(model) -> dict:
         a["flops"] += r.flops
         a["bytes"] += r.bytes
         if r.kind == 0:
-            sh = shapes.setdefault((r.m, r.n, r.k), [0, 0.0, 0.0])
+            sh = shapes.setdefault((r.m, r.n, r.k, r.tile_n, r.ctas), [0, 0.0, 0.0])
             sh[0] += 1
             sh[1] += r.ms
             sh[2] += r.flops
     del lib
     top = sorted(shapes.items(), key=lambda kv: -kv[1][1])[:12]
-    agg["_gemm_shapes"] = [{"mnk": list(s), "launches": v[0], "ms": round(v[1], 3),
+    agg["_gemm_shapes"] = [{"mnk": list(s[:3]), "tile_n": s[3], "ctas": s[4], "launches": v[0], "ms": round(v[1], 3),
                             "tflops": round(v[2] / (v[1] * 1e-3) / 1e12, 1)} for s, v in top]
     return agg
 
@@ -480,7 +490,8 @@ def run_ours(args, rank, world, local):
         if top:
             ach = 2.0 * top["mnk"][0] * top["mnk"][1] * top["mnk"][2] * top["launches"] / (top["ms"] * 1e-3) / 1e12
             roofline = {"bound": "tensor",
-                        "kernel": f"gemm_bf16_tc_kernel M,N,K={top['mnk']} ({top['launches']} launches per step)",
+                        "kernel": (f"{'gemm_bf16_tc2_kernel' if top['ctas'] == 2 else 'gemm_bf16_tc_kernel'}<{top['tile_n']}> "
+                                   f"M,N,K={top['mnk']} ({top['launches']} launches per step)"),
                         "achieved": round(ach, 1), "peak": tflops_peak, "unit": "TFLOP/s",
                         "frac": round(ach / tflops_peak, 4), "traffic": traffic,
                         "traffic_note": "ncu dram read+write per launch, scaled by rows from the M=16384 capture "

@@ -90,7 +90,8 @@ int vla_sync_check(void);
 /* Device error word without clearing (0 = none). */
 int vla_peek_device_error(unsigned int* code);
 /* sizeof of the ABI structs, in the order vla_epilogue, vla_attention_args,
- * vla_llama_layer, vla_vision_layer, written to out[0..n); returns the count. */
+ * vla_llama_layer, vla_vision_layer, vla_profile_record, written to out[0..n);
+ * returns the count. */
 int vla_abi_sizes(int64_t* out, int32_t n);
 /* Number of kernel launches this library has issued in this process (all
  * devices, all threads); a graph replay re-runs captured launches without
@@ -123,7 +124,9 @@ typedef struct vla_profile_record {
   float ms;
   double flops;
   double bytes;
-  int64_t m, n, k; /* GEMM problem shape (0 for other kinds) */
+  int64_t m, n, k;  /* GEMM problem shape (0 for other kinds) */
+  int32_t tile_n;   /* GEMM: output tile width BN */
+  int32_t ctas;     /* GEMM: CTAs per output tile (1, or 2 for a cta_group::2 pair) */
 } vla_profile_record;
 int vla_profile_start(int32_t capacity);
 int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count);
@@ -148,6 +151,14 @@ int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
 int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
                         int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, vla_stream_t stream);
 
+
+/* The GEMM with its schedule chosen by the caller: tile_n = N tile width
+ * (multiple of 32 in [32, 256], 0 = automatic) and ctas = 1 (one CTA per
+ * 128 x tile_n tile), 2 (a two-CTA cluster per 256 x tile_n tile, tile_n >= 64:
+ * each CTA stages its own A rows and half of the B tile, the pair's MMAs are
+ * issued by one CTA as tcgen05.mma.cta_group::2) or 0 (automatic). */
+int vla_gemm_bf16_ex(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                     int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, int32_t ctas, vla_stream_t stream);
 
 /* Row normalisation over bf16 rows of width N (N % 8 == 0), fp32 statistics.
  * RMSNorm:  y = x * rsqrt(mean(x^2) + eps) * g

@@ -32,10 +32,11 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 
 def test_abi_struct_sizes_match_ctypes():
-    out = (ctypes.c_int64 * 4)()
-    assert _lib.load().vla_abi_sizes(out, 4) == 4
+    out = (ctypes.c_int64 * 5)()
+    assert _lib.load().vla_abi_sizes(out, 5) == 5
     assert list(out) == [ctypes.sizeof(_lib.Epilogue), ctypes.sizeof(_lib.AttentionArgs),
-                         ctypes.sizeof(_lib.LlamaLayer), ctypes.sizeof(_lib.VisionLayer)]
+                         ctypes.sizeof(_lib.LlamaLayer), ctypes.sizeof(_lib.VisionLayer),
+                         ctypes.sizeof(_lib.ProfileRecord)]
 
 
 def test_host_validation_without_gpu():

@@ -56,3 +56,60 @@ def test_gemm_16_column_tails(cuda, N):
         ref = a.float() @ w.float().T + bias.float() + res.float()
         torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=2e-2)
         assert (buf[:, N:] == 7.0).all(), "columns beyond N were written"
+
+
+@pytest.mark.parametrize("tile_n", [64, 96, 128, 160, 192, 224, 256])
+@pytest.mark.parametrize("M,N,K", [(1024, 768, 768), (1000, 720, 720), (300, 1600, 960), (4096, 256, 64)])
+def test_gemm_cta_pair(cuda, tile_n, M, N, K):
+    """Two-CTA (cta_group::2) kernel: 256-row tiles split over a CTA pair, each CTA
+    staging its own A rows and half of B; M tails leave part of (or all of) the
+    second CTA's rows empty; bias + residual epilogue with a 16-column N tail."""
+    from vla_b200 import device as dev
+    g = torch.Generator().manual_seed(M + N + K + tile_n)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    bias = torch.randn(N, generator=g).to(torch.bfloat16).cuda()
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16).cuda()
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a, w, out, dev.make_epilogue(bias=bias, residual=res), tile_n=tile_n, ctas=2)
+    dev.sync_check()
+    ref = a.float() @ w.float().T + bias.float() + res.float()
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=2e-2)
+
+
+def test_gemm_cta_pair_epilogues(cuda):
+    """GELU, SwiGLU, RoPE and row-scatter epilogues on the CTA-pair kernel."""
+    import torch.nn.functional as F
+    from oracle import smolvla_ref as R
+    from vla_b200 import _lib, device as dev
+    from vla_b200.model import interleave_gate_up, rope_table
+    g = torch.Generator().manual_seed(5)
+    M, K = 700, 192
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(256, K, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(256, generator=g) * 0.1).to(torch.bfloat16)
+    out = torch.empty(M, 256, dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a.cuda(), w.cuda(), out, dev.make_epilogue(bias=b.cuda(), act=_lib.ACT_GELU_TANH), ctas=2)
+    torch.testing.assert_close(out.float().cpu(), F.gelu(a.float() @ w.float().T + b.float(), approximate="tanh"),
+                               atol=3e-2, rtol=2e-2)
+    wg, wu = (torch.randn(K, 320, generator=g) * 0.05).to(torch.bfloat16), \
+        (torch.randn(K, 320, generator=g) * 0.05).to(torch.bfloat16)
+    out = torch.empty(M, 320, dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a.cuda(), interleave_gate_up(wg, wu, "cuda"), out, dev.make_epilogue(act=_lib.ACT_SWIGLU), ctas=2)
+    torch.testing.assert_close(out.float().cpu(), F.silu(a.float() @ wg.float()) * (a.float() @ wu.float()),
+                               atol=3e-2, rtol=2e-2)
+    wq = (torch.randn(192, K, generator=g) * 0.05).to(torch.bfloat16)
+    cs = rope_table(50, 64, 1e4).cuda()
+    out = torch.empty(M, 192, dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a.cuda(), wq.cuda(), out, dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=128),
+             tile_n=64, ctas=2)
+    y = a.float() @ wq.float().T
+    pos = (torch.arange(M) % 50).float()
+    rot = R.apply_rope(y[:, :128].reshape(M, 1, 2, 64), 1e4, positions=pos[:, None]).reshape(M, 128)
+    torch.testing.assert_close(out.float().cpu(), torch.cat([rot, y[:, 128:]], 1), atol=3e-2, rtol=2e-2)
+    out = torch.zeros(M // 7 * 9, 256, dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a.cuda(), w.cuda(), out, dev.make_epilogue(out_grp=7, out_grp_stride=9), ctas=2)
+    o = out.view(M // 7, 9, 256).cpu()
+    torch.testing.assert_close(o[:, :7].float(), (a.float() @ w.float().T).view(M // 7, 7, 256), atol=3e-2, rtol=2e-2)
+    assert o[:, 7:].abs().sum() == 0
+    dev.sync_check()

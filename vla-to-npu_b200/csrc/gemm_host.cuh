@@ -2,6 +2,7 @@
 // tensor maps, persistent grid sizing (one CTA per SM).
 #pragma once
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "host_common.cuh"
 
 namespace vla {
@@ -25,6 +26,75 @@ static int choose_bn(int64_t M, int64_t N, int act, int num_sms) {
     }
   }
   return best;
+}
+
+// Largest number of co-resident 2-CTA clusters of the pair kernel<BN> (GPC
+// boundaries can leave SMs without a partner), cached per device and width.
+template <int BN>
+static int max_pair_clusters() {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (cached[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg2<BN>::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc2_kernel<BN>, &cfg) != cudaSuccess || n <= 0)
+      n = device_info().num_sms / 2;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN>
+static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const DevEpi& ep, int64_t M, int64_t N,
+                      int64_t K, cudaStream_t st) {
+  using Cf = Cfg2<BN>;
+  CUtensorMap tb;
+  int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN / 2);
+  if (rc) return rc;
+  static thread_local int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cf::SMEM_BYTES));
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+  const int clusters = max_pair_clusters<BN>();
+  const int grid = 2 * (int)(tiles < clusters ? tiles : clusters);
+  prof_begin(st);
+  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ep, (int)M,
+                   (int)N, (int)K);
+  {
+    const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
+    double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
+    if (ep.residual) bytes += 2.0 * M * out_cols;
+    if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 2);
+  }
+  return launch_status("gemm_bf16_tc2");
+}
+
+// One-CTA tile or CTA pair (gemm2.cuh).  The pair halves each SM's B staging
+// traffic and doubles the MMA's M; inside the full C4 step (B = 256) it measured
+// faster on B200 for every GEMM shape of the step (+3-25 % per shape).  Small M
+// (below 4096 rows, e.g. the single-observation blocks, where the pair lost
+// 3-10 %) stays on one CTA per tile.
+static int choose_ctas(int64_t M, int bn) {
+  return (M >= 32 * BM && bn >= 64) ? 2 : 1;
 }
 
 template <int BN>
@@ -52,13 +122,13 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const De
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
     if (ep.residual) bytes += 2.0 * M * out_cols;
     if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
-    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K);
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 1);
   }
   return launch_status("gemm_bf16_tc");
 }
 
 static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
-               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0) {
+               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0, int force_ctas = 0) {
   VLA_CHECK_ARG(A && B && C, "gemm: null operand");
   VLA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
                 (long long)K);
@@ -119,6 +189,27 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   int rc = make_tmap_bf16_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
   if (rc) return rc;
   const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
+  // VLA_GEMM_CTAS=1|2 overrides the automatic one-CTA / pair choice (A/B measurement)
+  static const int env_ctas = [] {
+    const char* v = getenv("VLA_GEMM_CTAS");
+    return v ? atoi(v) : 0;
+  }();
+  const int ctas = force_ctas                          ? force_ctas
+                   : (env_ctas == 1 || env_ctas == 2) ? env_ctas
+                                                      : choose_ctas(M, bn);
+  if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
+  if (ctas == 2) {
+    switch (bn) {
+      case 256: return launch_bn2<256>(ta, B, ldb, ep, M, N, K, st);
+      case 224: return launch_bn2<224>(ta, B, ldb, ep, M, N, K, st);
+      case 192: return launch_bn2<192>(ta, B, ldb, ep, M, N, K, st);
+      case 160: return launch_bn2<160>(ta, B, ldb, ep, M, N, K, st);
+      case 128: return launch_bn2<128>(ta, B, ldb, ep, M, N, K, st);
+      case 96: return launch_bn2<96>(ta, B, ldb, ep, M, N, K, st);
+      case 64: return launch_bn2<64>(ta, B, ldb, ep, M, N, K, st);
+      default: return set_error(VLA_E_UNSUPPORTED, "gemm: pair tile width %d not built", bn);
+    }
+  }
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, ep, M, N, K, st);
     case 224: return launch_bn<224>(ta, B, ldb, ep, M, N, K, st);

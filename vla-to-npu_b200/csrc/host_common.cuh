@@ -117,6 +117,27 @@ static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Same, for a kernel launched in clusters of `cluster_x` CTAs along x.
+template <typename... KArgs, typename... Args>
+static void launch_k_cluster(void (*kernel)(KArgs...), int cluster_x, dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_launch_overlap.load(std::memory_order_relaxed) ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 static inline cudaStream_t as_stream(vla_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Number of kernels this library has launched in this process.
@@ -132,6 +153,7 @@ struct ProfRec {
   double flops, bytes;
   cudaEvent_t a, b;
   int64_t m, n, k;
+  int tile_n, ctas;
 };
 struct Profiler {
   bool on = false;
@@ -148,11 +170,11 @@ static inline void prof_begin(cudaStream_t st) {
   cudaEventRecord(g_prof.pending, st);
 }
 static inline void prof_end(cudaStream_t st, int kind, double flops, double bytes, int64_t m = 0, int64_t n = 0,
-                            int64_t k = 0) {
+                            int64_t k = 0, int tile_n = 0, int ctas = 0) {
   if (!g_prof.on || g_prof.pending == nullptr || g_prof.next + 1 > g_prof.pool.size()) return;
   cudaEvent_t e = g_prof.pool[g_prof.next++];
   cudaEventRecord(e, st);
-  g_prof.recs.push_back(ProfRec{kind, flops, bytes, g_prof.pending, e, m, n, k});
+  g_prof.recs.push_back(ProfRec{kind, flops, bytes, g_prof.pending, e, m, n, k, tile_n, ctas});
   g_prof.pending = nullptr;
 }
 

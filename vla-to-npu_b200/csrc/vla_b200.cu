@@ -100,6 +100,8 @@ int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count) 
       out[n].m = r.m;
       out[n].n = r.n;
       out[n].k = r.k;
+      out[n].tile_n = r.tile_n;
+      out[n].ctas = r.ctas;
     }
     ++n;
   }
@@ -111,10 +113,11 @@ int vla_profile_stop(vla_profile_record* out, int32_t capacity, int32_t* count) 
 }
 
 int vla_abi_sizes(int64_t* out, int32_t n) {
-  const int64_t sz[4] = {(int64_t)sizeof(vla_epilogue), (int64_t)sizeof(vla_attention_args),
-                         (int64_t)sizeof(vla_llama_layer), (int64_t)sizeof(vla_vision_layer)};
-  for (int i = 0; i < n && i < 4; ++i) out[i] = sz[i];
-  return 4;
+  const int64_t sz[5] = {(int64_t)sizeof(vla_epilogue), (int64_t)sizeof(vla_attention_args),
+                         (int64_t)sizeof(vla_llama_layer), (int64_t)sizeof(vla_vision_layer),
+                         (int64_t)sizeof(vla_profile_record)};
+  for (int i = 0; i < n && i < 5; ++i) out[i] = sz[i];
+  return 5;
 }
 
 int vla_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
@@ -126,6 +129,15 @@ int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, 
                         int64_t N, int64_t K, const vla_epilogue* epi, int tile_n, vla_stream_t stream) {
   VLA_CHECK_ARG(tile_n >= 32 && tile_n <= 256 && tile_n % 32 == 0, "tile_n must be a multiple of 32 in [32, 256]");
   return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n);
+}
+
+int vla_gemm_bf16_ex(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                     int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, int32_t ctas, vla_stream_t stream) {
+  VLA_CHECK_ARG(tile_n == 0 || (tile_n >= 32 && tile_n <= 256 && tile_n % 32 == 0),
+                "tile_n must be 0 or a multiple of 32 in [32, 256]");
+  VLA_CHECK_ARG(ctas >= 0 && ctas <= 2, "ctas must be 0 (auto), 1 or 2");
+  VLA_CHECK_ARG(ctas != 2 || tile_n == 0 || tile_n >= 64, "a CTA pair needs tile_n >= 64");
+  return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n, ctas);
 }
 
 int vla_rms_norm_bf16(const void* x, int64_t ldx, const void* g, void* y, int64_t ldy, int64_t M, int64_t N, float eps,

@@ -104,7 +104,8 @@ class ProfileRecord(ctypes.Structure):
     """Mirror of ``vla_profile_record``."""
 
     _fields_ = [("kind", ctypes.c_int32), ("ms", ctypes.c_float), ("flops", ctypes.c_double),
-                ("bytes", ctypes.c_double), ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64)]
+                ("bytes", ctypes.c_double), ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+                ("tile_n", ctypes.c_int32), ("ctas", ctypes.c_int32)]
 
 
 KIND_NAMES = ["gemm", "attention", "norm", "rope", "softmax", "elementwise", "layout"]
@@ -127,6 +128,7 @@ SIGNATURES = {
     "vla_profile_stop": [ctypes.POINTER(ProfileRecord), _I32, ctypes.POINTER(ctypes.c_int32)],
     "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
     "vla_gemm_bf16_tiled": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _P],
+    "vla_gemm_bf16_ex": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _I32, _P],
     "vla_rms_norm_bf16": [_P, _I64, _P, _P, _I64, _I64, _I64, _F32, _P],
     "vla_layer_norm_bf16": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _F32, _P],
     "vla_rope_bf16": [_P, _I64, _I64, _I32, _I32, _P, _P],
