@@ -59,6 +59,7 @@ def parse_args():
                          + ", ".join(KERNEL_CASES))
     ap.add_argument("--ctas", type=int, default=0, choices=[0, 1, 2],
                     help="GEMM kernel cases: force one CTA (1) or a CTA pair (2) per tile; 0 = automatic")
+    ap.add_argument("--tile-n", type=int, default=0, help="GEMM kernel cases: force the tile width BN; 0 = automatic")
     return ap.parse_args()
 
 
@@ -72,6 +73,8 @@ KERNEL_CASES = {
     "gemm_plain_k3072": "plain GEMM, M=16384 N=3072 K=3072",
     "gemm_exp_down": "action-expert down projection + residual, M=12800 N=720 K=2048",
     "gemm_exp_o": "action-expert output projection + residual, M=12800 N=720 K=960",
+    "gemm_exp_qkv": "action-expert self-attention QKV + RoPE on Q and K, M=12800 N=1600 K=720",
+    "gemm_exp_gu": "action-expert gate/up + SwiGLU, M=12800 N=4096 K=720",
     "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
     "layer_norm": "SigLIP LayerNorm, 16384 x 768",
 }
@@ -90,17 +93,25 @@ def run_kernel_case(args):
         M, N, K = {"gemm_fc1": (16384, 3072, 768), "gemm_qkv": (16384, 2304, 768),
                    "gemm_fc2": (16384, 768, 3072), "gemm_plain": (16384, 3072, 768),
                    "gemm_plain_k3072": (16384, 3072, 3072), "gemm_exp_down": (12800, 720, 2048),
-                   "gemm_exp_o": (12800, 720, 960)}[name]
+                   "gemm_exp_o": (12800, 720, 960), "gemm_exp_qkv": (12800, 1600, 720),
+                   "gemm_exp_gu": (12800, 4096, 720)}[name]
         a = W.randn((M, K), 0, "kc.a").cuda()
         w = W.randn((N, K), 0, "kc.w", std=0.02).cuda()
         b = W.randn((N,), 0, "kc.b", std=0.01).cuda()
-        c = torch.empty(M, N, dtype=bf, device="cuda")
+        c = torch.empty(M, N // 2 if name == "gemm_exp_gu" else N, dtype=bf, device="cuda")
         res = W.randn((M, N), 0, "kc.r").cuda() if name in ("gemm_fc2", "gemm_exp_down", "gemm_exp_o") else None
         plain = name.startswith("gemm_plain") or name.startswith("gemm_exp")
         epi = dev.make_epilogue(bias=None if plain else b, residual=res,
                                 act=_lib.ACT_GELU_TANH if name == "gemm_fc1" else 0)
-        fn = lambda: dev.gemm(a, w, c, epi, ctas=args.ctas)  # noqa: E731
-        flops, nbytes = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * N * (2 if res is not None else 1))
+        if name == "gemm_exp_qkv":
+            from vla_b200.model import rope_table
+            cs = rope_table(50, 64, 10_000.0).cuda()
+            epi = dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=1280)
+        elif name == "gemm_exp_gu":
+            epi = dev.make_epilogue(act=_lib.ACT_SWIGLU)
+        fn = lambda: dev.gemm(a, w, c, epi, tile_n=args.tile_n, ctas=args.ctas)  # noqa: E731
+        out_cols = c.shape[1]
+        flops, nbytes = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * out_cols * (2 if res is not None else 1))
     elif name == "attn_vision":
         B, L, H = 16, 1024, 12
         qkv = W.randn((B * L, 3 * H * 64), 0, "kc.qkv").cuda()

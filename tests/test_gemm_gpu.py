@@ -113,3 +113,31 @@ def test_gemm_cta_pair_epilogues(cuda):
     torch.testing.assert_close(o[:, :7].float(), (a.float() @ w.float().T).view(M // 7, 7, 256), atol=3e-2, rtol=2e-2)
     assert o[:, 7:].abs().sum() == 0
     dev.sync_check()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ctas", [1, 2])
+@pytest.mark.parametrize("tile_n", [64, 128, 192, 256])
+def test_gemm_rope_tile_widths(cuda, tile_n, ctas):
+    """RoPE epilogue (+bias, +residual) where a tile holds several heads and the
+    rotated-column boundary (rope_ncols) falls inside a tile."""
+    from oracle import smolvla_ref as R
+    from vla_b200 import _lib, device as dev
+    from vla_b200.model import rope_table
+    g = torch.Generator().manual_seed(11)
+    M, K, N, nrot, seq = 4200, 160, 448, 320, 50
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    r = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    cs = rope_table(seq, 64, 1e4).cuda()
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a.cuda(), w.cuda(), out, dev.make_epilogue(bias=b.cuda(), residual=r.cuda(), act=_lib.ACT_ROPE,
+                                                        rope_cs=cs, rope_seq=seq, rope_ncols=nrot),
+             tile_n=tile_n, ctas=ctas)
+    y = a.float() @ w.float().T + b.float()
+    pos = (torch.arange(M) % seq).float()
+    rot = R.apply_rope(y[:, :nrot].reshape(M, 1, nrot // 64, 64), 1e4, positions=pos[:, None]).reshape(M, nrot)
+    ref = torch.cat([rot, y[:, nrot:]], 1) + r.float()
+    torch.testing.assert_close(out.float().cpu(), ref, atol=4e-2, rtol=2e-2)
+    dev.sync_check()

@@ -156,68 +156,88 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
     if (i < nv) cp[i] = pack_bf16x8(v + 8 * i);
 }
 
-// RoPE on one 64-wide head [n, n+64) of row m: rotate pairs (d, d+32), d < 32,
-// in two 16-pair halves (cos / sin read as float4 from the [pos][64] table).
-__device__ __forceinline__ void rope_head(const DevEpi& ep, uint32_t taddr, int m, int n, long long orow,
-                                          bool row_ok) {
-  const bool rot = n < ep.rope_ncols;
+// RoPE epilogue of row m over the 64-wide heads of a BN-wide tile: rotate pairs
+// (d, d+32), d < 32.  The pairs split into two halves (d < 16, d >= 16); with an
+// even number of warps per lane quarter each warp owns one half of every head it
+// visits, so it loads that half's 16 cos + 16 sin of row m's position once per
+// tile and reuses them for all heads (every thread reads its own table row, so
+// each table load touches 32 cache lines: reloading it per head made the RoPE
+// GEMMs bound by L1 wavefronts).
+template <int BN>
+__device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, long long orow,
+                                          bool row_ok, int part, int nparts) {
+  const bool split = (nparts & 1) == 0;
+  const int hq0 = split ? (part & 1) : 0;
+  const int hq1 = split ? (part & 1) : 1;
+  const int h0 = split ? (part >> 1) : part;
+  const int hstep = split ? (nparts >> 1) : nparts;
   const float* cs = ep.rope_cs + (long long)(m % ep.rope_seq) * 64;
+#pragma unroll 1
+  for (int hq = hq0; hq <= hq1; ++hq) {
+    float cc[16], ss[16];
+    bool have_cs = false;
+#pragma unroll 1
+    for (int h = h0; h < BN / 64; h += hstep) {
+      const int n = n0 + 64 * h;
+      if (n >= ep.N) break;
+      float lo[16], hi[16];
+      tmem_ld16x2(taddr + 64 * h + 16 * hq, taddr + 64 * h + 32 + 16 * hq, lo, hi);
+      if (!row_ok) continue;
 #pragma unroll
-  for (int hq = 0; hq < 2; ++hq) {
-    float lo[16], hi[16];
-    tmem_ld16(taddr + 16 * hq, lo);
-    tmem_ld16(taddr + 32 + 16 * hq, hi);
-    if (!row_ok) continue;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      lo[i] *= ep.alpha;
-      hi[i] *= ep.alpha;
-    }
-    if (ep.bias != nullptr) {
-      float b[8];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 16 * hq) + i), b);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) lo[8 * i + e] += b[e];
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 32 + 16 * hq) + i), b);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) hi[8 * i + e] += b[e];
+      for (int i = 0; i < 16; ++i) {
+        lo[i] *= ep.alpha;
+        hi[i] *= ep.alpha;
       }
-    }
-    if (rot) {
-      const float4* c4 = reinterpret_cast<const float4*>(cs + 16 * hq);
-      const float4* s4 = reinterpret_cast<const float4*>(cs + 32 + 16 * hq);
+      if (ep.bias != nullptr) {
+        float b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 c = __ldg(c4 + i), sn = __ldg(s4 + i);
-        const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+        for (int i = 0; i < 2; ++i) {
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 16 * hq) + i), b);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = lo[4 * i + e], b = hi[4 * i + e];
-          lo[4 * i + e] = a * cc[e] - b * ss[e];
-          hi[4 * i + e] = b * cc[e] + a * ss[e];
+          for (int e = 0; e < 8; ++e) lo[8 * i + e] += b[e];
+          unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(ep.bias + n + 32 + 16 * hq) + i), b);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hi[8 * i + e] += b[e];
         }
       }
-    }
-    if (ep.residual != nullptr) {
-      const bf16* rp = ep.residual + res_row(ep, m) * ep.ldr + n;
-      float r[8];
+      if (n < ep.rope_ncols) {
+        if (!have_cs) {
+          const float4* c4 = reinterpret_cast<const float4*>(cs + 16 * hq);
+          const float4* s4 = reinterpret_cast<const float4*>(cs + 32 + 16 * hq);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 16 * hq)[i], r);
+          for (int i = 0; i < 4; ++i) {
+            const float4 c = __ldg(c4 + i), sn = __ldg(s4 + i);
+            cc[4 * i] = c.x, cc[4 * i + 1] = c.y, cc[4 * i + 2] = c.z, cc[4 * i + 3] = c.w;
+            ss[4 * i] = sn.x, ss[4 * i + 1] = sn.y, ss[4 * i + 2] = sn.z, ss[4 * i + 3] = sn.w;
+          }
+          have_cs = true;
+        }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) lo[8 * i + e] += r[e];
-        unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 32 + 16 * hq)[i], r);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) hi[8 * i + e] += r[e];
+        for (int e = 0; e < 16; ++e) {
+          const float a = lo[e], b = hi[e];
+          lo[e] = a * cc[e] - b * ss[e];
+          hi[e] = b * cc[e] + a * ss[e];
+        }
       }
+      if (ep.residual != nullptr) {
+        const bf16* rp = ep.residual + res_row(ep, m) * ep.ldr + n;
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 16 * hq)[i], r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) lo[8 * i + e] += r[e];
+          unpack_bf16x8(reinterpret_cast<const uint4*>(rp + 32 + 16 * hq)[i], r);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hi[8 * i + e] += r[e];
+        }
+      }
+      bf16* cp = ep.C + orow * ep.ldc + n;
+      reinterpret_cast<uint4*>(cp + 16 * hq)[0] = pack_bf16x8(lo);
+      reinterpret_cast<uint4*>(cp + 16 * hq)[1] = pack_bf16x8(lo + 8);
+      reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[0] = pack_bf16x8(hi);
+      reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[1] = pack_bf16x8(hi + 8);
     }
-    bf16* cp = ep.C + orow * ep.ldc + n;
-    reinterpret_cast<uint4*>(cp + 16 * hq)[0] = pack_bf16x8(lo);
-    reinterpret_cast<uint4*>(cp + 16 * hq)[1] = pack_bf16x8(lo + 8);
-    reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[0] = pack_bf16x8(hi);
-    reinterpret_cast<uint4*>(cp + 32 + 16 * hq)[1] = pack_bf16x8(hi + 8);
   }
 }
 
@@ -229,12 +249,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
-#pragma unroll 1
-    for (int h = 64 * part; h < BN; h += 64 * nparts) {
-      const int n = n0 + h;
-      if (n >= ep.N) break;
-      rope_head(ep, taddr + h, m, n, orow, row_ok);
-    }
+    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts);
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
     for (int c = 32 * part; c < BN; c += 32 * nparts) {
