@@ -6,16 +6,23 @@
 //              128 keys into separate 3-stage rings (K is released as soon as
 //              S = Q K^T completes, V after P.V)
 //   warp 1     TMEM allocator + single-thread MMA issuer:
-//                S_j  = Q . K_j^T   (UMMA 128x128x16, A = Q, B = K, both K-major)
-//                PV_j = P_j . V_j   (UMMA 128x64x16, A = P from tensor memory,
-//                                    B = V from smem MN-major, no transpose pass)
+//                S_j  = Q . K_j^T         (UMMA 128x128x16, A = Q, B = K, both K-major)
+//                O   += P_j . [V_j | 1]   (UMMA 128x80x16, A = P from tensor memory,
+//                                          B = V from smem MN-major, no transpose pass)
 //   warps 2..5 softmax: thread r owns query row r; reads its S row from TMEM
-//              (so row max / sum need no shuffles), P = exp2(S*scale*log2e - m)
+//              (so the row max needs no shuffles), P = exp2(S*scale*log2e - m)
 //              rounded to bf16 and stored back into the S columns of TMEM (no
-//              shared-memory round trip) for the P.V MMA, and keeps the
-//              output row O (64 fp32) in registers: O = O*alpha + PV.
-// S is double-buffered in TMEM (S_{j+1} is computed while row j is in softmax),
-// P and PV are double-buffered too.  TMEM: 2 x 128 (S) + 2 x 64 (PV) columns.
+//              shared-memory round trip) for the P.V MMA.
+// The output accumulator O lives in TMEM (double-buffered across items) and is
+// accumulated by the tensor core over the item's key tiles.  The B operand of
+// P.V is V extended by a 16-column block of ones (a constant smem block reached
+// through the descriptor's leading byte offset), so O column 64 accumulates the
+// row sum of P: the softmax threads neither add up P nor touch O per tile.  The
+// running max m only moves when a row's max grows by more than 2^8 (log2 units),
+// and only then is that row of O rescaled in TMEM (P values stay below 2^8,
+// exact in fp32 and bf16 alike).
+// S is double-buffered in TMEM (S_{j+1} is computed while row j is in softmax).
+// TMEM: 2 x 128 (S) + 2 x 80 (O | row sum) columns.
 //
 // Used for the non-causal SigLIP attention (1024 keys per head); the small
 // text / expert attentions run on the mma.sync kernel (attention.cuh).
@@ -33,8 +40,10 @@ constexpr int kVStages = 3;
 constexpr int kThreads = 192;
 constexpr int TILE_BYTES = BKV * HD * 2;  // 16 KB: a [128 x 64] bf16 tile (Q, K or V)
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL0 = 0;     // S buffers at columns 0 and 128
-constexpr uint32_t PV_COL0 = 256;  // PV buffers at columns 256 and 320
+constexpr uint32_t S_COL0 = 0;    // S buffers at columns 0 and 128
+constexpr uint32_t O_COL0 = 256;  // O buffers at columns 256 and 336
+constexpr int ON = HD + 16;       // O columns: 64 outputs + 16 copies of the row sum
+constexpr float kRescaleLog2 = 8.f;
 
 struct Params {
   int Lq, Lk, Hq, Hkv, batch;
@@ -50,10 +59,12 @@ struct Smem {
   uint8_t q[2][TILE_BYTES];
   uint8_t k[kKStages][TILE_BYTES];
   uint8_t v[kVStages][TILE_BYTES];
+  uint8_t ones[TILE_BYTES];  // bf16 1.0: the extra N atom of every P.V B operand
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
-  uint64_t s_full[2], p_full[2], pv_full[2], pv_empty[2];
+  uint64_t s_full[2], p_full[2], o_empty[2];
+  uint64_t pv_done;  // completes once per P.V, in the CTA's tile order
   uint32_t tmem_base;
   int abort;
 };
@@ -62,6 +73,23 @@ __device__ __forceinline__ float ex2_fast(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns from registers, then wait.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
 // 32 lanes x 64 consecutive 32-bit TMEM columns from registers, then wait.
@@ -96,12 +124,13 @@ __device__ __forceinline__ void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem,
 }
 
 // MN-major SW128 descriptor for a [rows x 64] bf16 tile read along the row
-// (K) direction: 8-row groups 1024 bytes apart (stride byte offset), a single
-// 64-element atom along N.
-__device__ __forceinline__ uint64_t make_sw128_mn_desc(uint32_t smem_addr) {
+// (K) direction: 8-row groups 1024 bytes apart (stride byte offset); the next
+// 64-element atom along N starts `next_atom` bytes after this one (leading
+// byte offset), which is where the ones block sits for the N = 80 P.V MMA.
+__device__ __forceinline__ uint64_t make_sw128_mn_desc(uint32_t smem_addr, uint32_t next_atom) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(16384u >> 4) << 16;  // leading byte offset: next N atom (unused for N = 64)
+  d |= (uint64_t)((next_atom >> 4) & 0x3FFFu) << 16;  // leading byte offset: next N atom
   d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset: next 8 K-rows
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
@@ -140,9 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.q_empty[i], 1);
       mbar_init(&sm.s_full[i], 1);
       mbar_init(&sm.p_full[i], 128);
-      mbar_init(&sm.pv_full[i], 1);
-      mbar_init(&sm.pv_empty[i], 128);
+      mbar_init(&sm.o_empty[i], 128);
     }
+    mbar_init(&sm.pv_done, 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_empty[s], 1);
@@ -155,6 +184,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(&sm.tmem_base, TMEM_COLS);
+  {
+    // the ones block, written through the generic proxy and read by the tensor core
+    uint4* o4 = reinterpret_cast<uint4*>(sm.ones);
+    const uint4 one8 = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    for (int i = threadIdx.x; i < TILE_BYTES / 16; i += kThreads) o4[i] = one8;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -215,18 +251,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, HD) | (1u << 16);  // B (V) is MN-major
+      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, ON) | (1u << 16);  // B (V | 1) is MN-major
+      const uint32_t ones = smem_u32(sm.ones);
       bool ok = true;
-      int t = 0, it = 0;
+      int t = 0, it = 0, io = 0;  // tiles, items, items with at least one key tile
       for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++it) {
         int qt, h, b;
         item_coords(p, w, qt, h, b);
         const int n = (item_keys(p, b) + BKV - 1) / BKV;
         const int qb = it & 1;
         ok = mbar_wait_bounded(&sm.q_full[qb], (it >> 1) & 1, abort_flag);
+        if (!ok) break;
+        const int ob = io & 1;
         const uint64_t qdesc = make_sw128_desc(smem_u32(sm.q[qb]));
         // S of tile j, then P.V of tile j-1; finally P.V of the item's last tile
-        for (int j = 0; ok && j <= n; ++j) {
+        for (int j = 0; ok && j <= n && n > 0; ++j) {
           if (j < n) {
             const int tt = t + j;
             const int sk = tt % kKStages;
@@ -245,27 +284,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= 1) {
             const int tp = t + j - 1;
             const int sv = tp % kVStages;
-            ok = mbar_wait_bounded(&sm.p_full[tp & 1], (tp >> 1) & 1, abort_flag);
-            if (ok && tp >= 2) ok = mbar_wait_bounded(&sm.pv_empty[tp & 1], ((tp - 2) >> 1) & 1, abort_flag);
+            // O buffer ob was last read out by the softmax for item io-2
+            if (j == 1 && io >= 2) ok = mbar_wait_bounded(&sm.o_empty[ob], ((io - 2) >> 1) & 1, abort_flag);
+            if (ok) ok = mbar_wait_bounded(&sm.p_full[tp & 1], (tp >> 1) & 1, abort_flag);
             if (ok) ok = mbar_wait_bounded(&sm.v_full[sv], (tp / kVStages) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             // P (bf16, packed in pairs) lives in the first 64 columns of S buffer tp%2
             const uint32_t pt = tmem + S_COL0 + (uint32_t)(tp & 1) * BKV;
             const uint32_t vbase = smem_u32(sm.v[sv]);
-            const uint32_t d = tmem + PV_COL0 + (uint32_t)(tp & 1) * HD;
+            const uint32_t d = tmem + O_COL0 + (uint32_t)ob * ON;
 #pragma unroll
             for (int k = 0; k < BKV / 16; ++k) {
-              const uint64_t bdesc = make_sw128_mn_desc(vbase + (uint32_t)k * 2048u);
-              tc_mma_bf16_ts(d, pt + (uint32_t)k * 8u, bdesc, idesc_pv, k > 0);
+              const uint32_t a = vbase + (uint32_t)k * 2048u;
+              const uint64_t bdesc = make_sw128_mn_desc(a, ones - vbase);
+              tc_mma_bf16_ts(d, pt + (uint32_t)k * 8u, bdesc, idesc_pv, (j > 1 || k > 0) ? 1u : 0u);
             }
-            tc_commit(&sm.pv_full[tp & 1]);
+            tc_commit(&sm.pv_done);
             tc_commit(&sm.v_empty[sv]);
           }
         }
         if (!ok) break;
         tc_commit(&sm.q_empty[qb]);  // every S of this item has been issued before this point
         t += n;
+        if (n > 0) ++io;
       }
       if (!ok) {
         if (!*abort_flag) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
@@ -278,90 +320,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     bool ok = true;
-    int t = 0;
-    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
-      int qt, h, b;
-      item_coords(p, w, qt, h, b);
-      const int Lk = item_keys(p, b);
-      const int n = (Lk + BKV - 1) / BKV;
-      float o[HD];
-#pragma unroll
-      for (int i = 0; i < HD; ++i) o[i] = 0.f;
-      float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-      for (int j = 0; j <= n; ++j) {
-        float alpha = 1.f;
-        if (j < n) {
-          const int tt = t + j;
-          ok = mbar_wait_bounded(&sm.s_full[tt & 1], (tt >> 1) & 1, abort_flag);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t sadr = tmem + lane_base + S_COL0 + (uint32_t)(tt & 1) * BKV;
-          const int key0 = j * BKV;
-          float s[BKV];
-          tmem_ld128(sadr, s);
-          // row max over raw scores with 8 independent accumulators (short dependency chains)
-          if (key0 + BKV > Lk) {
-#pragma unroll
-            for (int c = 0; c < BKV; ++c)
-              if (key0 + c >= Lk) s[c] = -INFINITY;
-          }
-          float mx8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) mx8[i] = s[i];
-#pragma unroll
-          for (int c = 8; c < BKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-#pragma unroll
-          for (int i = 1; i < 8; ++i) mx8[0] = fmaxf(mx8[0], mx8[i]);
-          const float mnew = fmaxf(m, mx8[0] * p.scale_log2);
-          const float mbase = mnew == -INFINITY ? 0.f : mnew;
-          alpha = ex2_fast(m - mbase);
-          m = mnew;
-          float rs8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
-          // P row (128 keys): exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2, packed
-          // as 64 bf16 pairs into the first 64 TMEM columns of this S buffer (the
-          // scores are already in registers); the P.V MMA reads it from there
-          uint32_t pk[BKV / 2];
-#pragma unroll
-          for (int c = 0; c < BKV; c += 2) {
-            const float e0 = ex2_fast(fmaf(s[c], p.scale_log2, -mbase));
-            const float e1 = ex2_fast(fmaf(s[c + 1], p.scale_log2, -mbase));
-            rs8[c & 7] += e0;
-            rs8[(c + 1) & 7] += e1;
-            pk[c >> 1] = pack_bf16x2(e0, e1);
-          }
-          tmem_st64(sadr, pk);
-          float rs = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) rs += rs8[i];
-          l = l * alpha + rs;
-          tc_fence_before();
-          mbar_arrive(&sm.p_full[tt & 1]);
-        }
-        if (j >= 1) {
-          const int tp = t + j - 1;
-          ok = mbar_wait_bounded(&sm.pv_full[tp & 1], (tp >> 1) & 1, abort_flag);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t padr = tmem + lane_base + PV_COL0 + (uint32_t)(tp & 1) * HD;
-          float pv[HD];
-          tmem_ld64(padr, pv);
-          tc_fence_before();
-          mbar_arrive(&sm.pv_empty[tp & 1]);
-#pragma unroll
-          for (int i = 0; i < HD; ++i) o[i] = o[i] * alpha_prev + pv[i];
-        }
-        alpha_prev = alpha;
-      }
-      if (!ok) break;
-      const int qrow = qt * BQ + row;
+    int t = 0, io = 0;
+    // the previous item's output is read out of TMEM while this item's first
+    // tile is in softmax (its P.V is then certainly done)
+    bool pending = false;
+    int pend_b = 0, pend_h = 0, pend_qt = 0, pend_ob = 0, pend_tp = 0;
+    auto finish_item = [&]() -> bool {
+      // completion of the item's last P.V; no later P.V can have completed, as it
+      // needs a P this thread has not yet released
+      bool good = mbar_wait_bounded(&sm.pv_done, (uint32_t)pend_tp & 1u, abort_flag);
+      good = __all_sync(0xffffffffu, good);
+      if (!good) return false;
+      tc_fence_after();
+      const uint32_t oadr = tmem + lane_base + O_COL0 + (uint32_t)pend_ob * ON;
+      float o[HD], lsum[16];
+      tmem_ld64(oadr, o);
+      tmem_ld16(oadr + HD, lsum);
+      tc_fence_before();
+      mbar_arrive(&sm.o_empty[pend_ob]);
+      const int qrow = pend_qt * BQ + row;
       if (qrow < p.Lq) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.o + (long long)b * p.o_batch + (long long)qrow * p.o_row +
-                                              (long long)h * HD);
+        const float inv = lsum[0] > 0.f ? 1.f / lsum[0] : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.o + (long long)pend_b * p.o_batch + (long long)qrow * p.o_row +
+                                              (long long)pend_h * HD);
 #pragma unroll
         for (int c8 = 0; c8 < HD / 8; ++c8) {
           float tv8[8];
@@ -370,8 +351,98 @@ __global__ void __launch_bounds__(kThreads, 1)
           dst[c8] = pack_bf16x8(tv8);
         }
       }
+      return true;
+    };
+    for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+      int qt, h, b;
+      item_coords(p, w, qt, h, b);
+      const int Lk = item_keys(p, b);
+      const int n = (Lk + BKV - 1) / BKV;
+      if (n == 0) {
+        const int qrow = qt * BQ + row;
+        if (qrow < p.Lq) {
+          uint4* dst = reinterpret_cast<uint4*>(p.o + (long long)b * p.o_batch + (long long)qrow * p.o_row +
+                                                (long long)h * HD);
+#pragma unroll
+          for (int c8 = 0; c8 < HD / 8; ++c8) dst[c8] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
+      const int ob = io & 1;
+      float m = -INFINITY;  // running max of S * scale * log2(e), moved in steps > kRescaleLog2
+      for (int j = 0; j < n; ++j) {
+        const int tt = t + j;
+        ok = mbar_wait_bounded(&sm.s_full[tt & 1], (tt >> 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t sadr = tmem + lane_base + S_COL0 + (uint32_t)(tt & 1) * BKV;
+        const int key0 = j * BKV;
+        float s[BKV];
+        tmem_ld128(sadr, s);
+        if (key0 + BKV > Lk) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c)
+            if (key0 + c >= Lk) s[c] = -INFINITY;
+        }
+        // row max with 8 independent three-input max chains
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < BKV; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = max3f(mx8[i], s[c + i], s[c + 8 + i]);
+        }
+        const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
+                         p.scale_log2;
+        const bool grow = mx > m + kRescaleLog2;
+        const float alpha = grow ? ex2_fast(m - mx) : 1.f;
+        if (grow) m = mx;
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+          // rescale this warp's rows of O (and the row sums) once P.V of tile tt-1 is done
+          ok = mbar_wait_bounded(&sm.pv_done, (uint32_t)(tt - 1) & 1u, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t oadr = tmem + lane_base + O_COL0 + (uint32_t)ob * ON;
+          float o[HD];
+          uint32_t u[HD];
+          tmem_ld64(oadr, o);
+#pragma unroll
+          for (int i = 0; i < HD; ++i) u[i] = __float_as_uint(o[i] * alpha);
+          tmem_st64(oadr, u);
+          tmem_ld16(oadr + HD, o);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i] * alpha);
+          tmem_st16(oadr + HD, u);
+        }
+        const float mbase = m == -INFINITY ? 0.f : m;
+        // P row (128 keys): exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2, packed
+        // as 64 bf16 pairs into the first 64 TMEM columns of this S buffer
+        uint32_t pk[BKV / 2];
+#pragma unroll
+        for (int c = 0; c < BKV; c += 2) {
+          const float e0 = ex2_fast(fmaf(s[c], p.scale_log2, -mbase));
+          const float e1 = ex2_fast(fmaf(s[c + 1], p.scale_log2, -mbase));
+          pk[c >> 1] = pack_bf16x2(e0, e1);
+        }
+        tmem_st64(sadr, pk);
+        if (j == 0 && pending) {
+          ok = finish_item();
+          if (!ok) break;
+          pending = false;
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[tt & 1]);
+      }
+      if (!ok) break;
+      pending = true;
+      pend_b = b, pend_h = h, pend_qt = qt, pend_ob = ob, pend_tp = t + n - 1;
       t += n;
+      ++io;
     }
+    if (ok && pending) ok = finish_item();
     if (!ok && lane == 0) {
       if (!*abort_flag) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
       *abort_flag = 1;
