@@ -65,7 +65,7 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
   tp.Hq = p.Hq;
   tp.Hkv = p.Hkv;
   tp.batch = batch;
-  tp.n_qt = (p.Lq + attn_tc::BQ - 1) / attn_tc::BQ;
+  tp.n_qt = (p.Lq + attn_tc::ITEM_ROWS - 1) / attn_tc::ITEM_ROWS;
   tp.q_rows_per_seq = q_rows;
   tp.k_rows_per_seq = k_rows;
   tp.o = p.o;
@@ -80,6 +80,15 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
   if (!(attr_dev_mask & (1 << (dev & 31)))) {
     VLA_CUDA_TRY(
         cudaFuncSetAttribute(attn_tc::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cudaFuncAttributes fa{};
+    VLA_CUDA_TRY(cudaFuncGetAttributes(&fa, attn_tc::flash_attn_tc_kernel));
+    // the in-kernel register split (setmaxnreg) hands out exactly the launch's
+    // registers: it is only sound at the register count it was sized for
+    if (fa.numRegs != attn_tc::kLaunchRegs || fa.maxThreadsPerBlock < attn_tc::kThreads)
+      return set_error(VLA_E_CUDA,
+                       "flash_attn_tc: built with %d registers/thread (%d threads per block); the register split "
+                       "needs exactly %d for %d threads",
+                       fa.numRegs, fa.maxThreadsPerBlock, attn_tc::kLaunchRegs, attn_tc::kThreads);
     attr_dev_mask |= 1 << (dev & 31);
   }
   const long long items = (long long)tp.n_qt * p.Hq * batch;
