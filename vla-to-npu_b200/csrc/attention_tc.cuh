@@ -22,7 +22,10 @@
 // computes S_g(j+1) while group g is still turning S_g(j) into P (a group
 // releases S_g as soon as it has read it), and P.V runs behind the softmax.
 // Each SM sub-partition runs two softmax warps (one per group), so the TMEM
-// loads, exp chains and barrier waits of one overlap the other's work.
+// loads, exp chains and barrier waits of one overlap the other's work.  The
+// two warps on a sub-partition pass a token so that their exp phases alternate
+// (MUFU.EX2 is the sub-partition's scarcest pipe: left alone the two groups
+// fall into step and both wait on it, then both leave it idle).
 // Registers: the block is launched at kLaunchRegs per thread; warpgroup 0
 // (producer, MMA, idle) gives most of its share to the two softmax warpgroups
 // with setmaxnreg (kLowRegs x 128 + kHighRegs x 256 = kLaunchRegs x 384), so a
@@ -61,6 +64,12 @@ constexpr uint32_t S_COL0 = 0;    // S_0, S_1 at columns 0 and 128
 constexpr uint32_t P_COL0 = 256;  // P_0, P_1 (bf16 pairs) at columns 256 and 320
 constexpr uint32_t O_COL0 = 384;  // O_0, O_1 at columns 384 and 448
 constexpr float kRescaleLog2 = 8.f;
+// One key pair in kPolyPeriod has its exponentials evaluated by ex2_poly
+// instead of MUFU.EX2 (0 = none).
+#ifndef VLA_ATTN_POLY_PERIOD
+#define VLA_ATTN_POLY_PERIOD 0
+#endif
+constexpr int kPolyPeriod = VLA_ATTN_POLY_PERIOD;
 
 struct Params {
   int Lq, Lk, Hq, Hkv, batch;
@@ -81,6 +90,7 @@ struct Smem {
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_free[2], p_full[2];  // per softmax group, once per key tile
   uint64_t pv_done[2];                       // per group: completes once per P.V, in tile order
+  uint64_t mufu_tok[2][4];  // [group][sub-partition]: the exp phase token of each softmax warp
   uint32_t tmem_base;
   int abort;
 };
@@ -89,6 +99,22 @@ __device__ __forceinline__ float ex2_fast(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA and integer pipes, for part of the exponentials (MUFU.EX2
+// issues 16 lanes per clock per SM, the FMA pipe 128): Cody-Waite split
+// x = j + f with j = floor(x) from a round-down add of 1.5 * 2^23, f in [0, 1),
+// 2^f from a cubic minimax fit (coefficients fitted for this kernel; relative
+// error below 7.5e-5, far under the 2^-9 rounding of the bf16 P it feeds), and
+// j added to the exponent field.  x is clamped at -127 (masked keys give
+// 2^-127, which is negligible next to the row maximum's 2^0 .. 2^8).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -127.f);
+  const float r = __fadd_rd(x, 12582912.f);  // 1.5 * 2^23 + floor(x), exact
+  const float f = x - (r - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.07802452f, f, 0.22606716f), f, 0.69583356f), f, 0.99992520f);
+  const int j = __float_as_int(r) - 0x4B400000;
+  return __int_as_float(__float_as_int(p) + (j << 23));
 }
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -223,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.s_free[i], 128);
       mbar_init(&sm.p_full[i], 128);
       mbar_init(&sm.pv_done[i], 1);
+      for (int q = 0; q < 4; ++q) mbar_init(&sm.mufu_tok[i][q], 1);
     }
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(&sm.k_full[s], 1);
@@ -459,28 +486,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float mbase = m == -INFINITY ? 0.f : m;
+        // the exp phase of tile tt: group 0 goes first (its first wait passes on
+        // the fresh barrier), then the two groups alternate
+        ok = mbar_wait_bounded(&sm.mufu_tok[g][q], g == 0 ? (((uint32_t)tt & 1u) ^ 1u) : ((uint32_t)tt & 1u),
+                               abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
         // P = exp2(s * scale*log2e - m) as one FFMA + MUFU.EX2, packed as bf16
-        // pairs (keys 2c, 2c+1 in column c) and stored in two halves; row sum
-        // in 8 partial accumulators
+        // pairs (keys 2c, 2c+1 in column c); row sum in 8 partial accumulators
         float rs8[8];
+        uint32_t pk[BKV / 2];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t pk[BKV / 4];
-#pragma unroll
-          for (int c = 0; c < BKV / 2; c += 2) {
-            const float e0 = ex2_fast(fmaf(sr[hh * (BKV / 2) + c], p.scale_log2, -mbase));
-            const float e1 = ex2_fast(fmaf(sr[hh * (BKV / 2) + c + 1], p.scale_log2, -mbase));
-            if (hh == 0 && c < 8) {
-              rs8[c & 7] = e0;
-              rs8[(c + 1) & 7] = e1;
-            } else {
-              rs8[c & 7] += e0;
-              rs8[(c + 1) & 7] += e1;
-            }
-            pk[c >> 1] = pack_bf16x2(e0, e1);
+        for (int c = 0; c < BKV; c += 2) {
+          const float x0 = fmaf(sr[c], p.scale_log2, -mbase);
+          const float x1 = fmaf(sr[c + 1], p.scale_log2, -mbase);
+          const bool poly = kPolyPeriod > 0 && ((c >> 1) % (kPolyPeriod > 0 ? kPolyPeriod : 1)) == 0;
+          const float e0 = poly ? ex2_poly(x0) : ex2_fast(x0);
+          const float e1 = poly ? ex2_poly(x1) : ex2_fast(x1);
+          if (c < 8) {
+            rs8[c & 7] = e0;
+            rs8[(c + 1) & 7] = e1;
+          } else {
+            rs8[c & 7] += e0;
+            rs8[(c + 1) & 7] += e1;
           }
-          tmem_st32(p_adr + (uint32_t)hh * (BKV / 4), pk);
+          pk[c >> 1] = pack_bf16x2(e0, e1);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.mufu_tok[g ^ 1][q]);  // the other group's warp on this sub-partition
+        tmem_st32(p_adr, pk);
+        tmem_st32(p_adr + BKV / 4, pk + BKV / 4);
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         tc_fence_before();
         mbar_arrive(&sm.p_full[g]);
