@@ -8,8 +8,13 @@
 //               (UMMA 128 x BN x 16, fp32 accumulators in tensor memory,
 //               double-buffered so the epilogue of tile i overlaps the
 //               mainloop of tile i+1)
-// warps 2..5  : epilogue — tcgen05.ld 32 lanes x 16 columns, fused bias /
-//               GELU-tanh / SwiGLU / RoPE / Euler / residual, bf16 stores.
+// warps 2..9  : epilogue — tcgen05.ld 32 lanes x 16 columns, fused bias /
+//               GELU-tanh / SwiGLU / RoPE / Euler / residual.  Output chunks
+//               of 32 rows x 32 columns go through a per-warp shared-memory
+//               staging buffer and a TMA tensor store (full-line global writes;
+//               direct per-row stores touch 32 lines per warp instruction and
+//               made the epilogue the bound of short-K GEMMs); RoPE, Euler and
+//               row-scatter epilogues store directly.
 //
 // This is the replacement for the reference's Allo GEMM module plus the host
 // loops that sum its bf16 K-chunks (vla/text_encoder_bf16.py:583-590,
@@ -44,17 +49,70 @@ struct DevEpi {
   float* euler_x;
   long long ldx;
   float euler_dt;
+  int tma_c;  // stores go through shared memory and the C tensor map
   int M, N;
 };
+
+// Per-warp output staging for the TMA store: two 2 KB buffers (32 rows x 64 B),
+// used alternately; one bulk-async group per stored chunk.
+constexpr int kStageC = 32 * 64;
+constexpr int kEpiStoreBytes = kEpiWarps * 2 * kStageC;
+constexpr int kSmemLimit = 232448;  // dynamic shared memory per block on sm_100
+
+struct EpiStore {
+  uint32_t buf;  // shared address of this warp's two staging buffers
+  int sb;        // buffer the next chunk uses
+  int row0;      // output row of the warp's lane 0
+};
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t smem, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem), "r"(x), "r"(y)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t a, const uint4& v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+
+// Stage this warp's 32 rows x (NVEC * 8) columns (lane = row) and store them
+// with TMA at column `col`.  The layout matches the tensor map's swizzle
+// (64-byte for 4 vectors a row, 32-byte for 2), which also keeps the 16-byte
+// shared stores of 8 consecutive rows on distinct banks.
+template <int NVEC>
+__device__ __forceinline__ void stage_store(const CUtensorMap* tm, EpiStore& es, const uint4* v, int lane, int col) {
+  const uint32_t b = es.buf + (uint32_t)es.sb * (uint32_t)kStageC;
+  // the store that last read this buffer (two chunks ago) must have finished reading
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NVEC; ++i) {
+    const int phys = NVEC == 4 ? (i ^ ((lane >> 1) & 3)) : (i ^ ((lane >> 2) & 1));
+    st_shared_v4(b + (uint32_t)(lane * NVEC * 16 + phys * 16), v[i]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) tma_store_2d(tm, b, col, es.row0);
+  es.sb ^= 1;
+}
+
+// All of this warp's TMA stores have completed (issued by lane 0).
+__device__ __forceinline__ void stage_drain(int lane) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  __syncwarp();
+}
 
 template <int BN>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) > 8 ? 8 : (200 * 1024 / STAGE_BYTES);
+  static constexpr int BUDGET = kSmemLimit - 1024 - 256 - kEpiStoreBytes;
+  static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + 256 + 1024;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (multiple of 32 for the epilogue chunks)");
   static_assert(B_BYTES % 1024 == 0, "B tile alignment");
 };
@@ -107,8 +165,10 @@ __device__ __forceinline__ void prefetch32(const DevEpi& ep, int m, int n, bool 
 }
 
 // Finish the chunk [n, n+32) (or its 16-column tail) of row m held in v[] (fp32, alpha applied).
+// With ep.tma_c every lane takes part (rows at or past M are clipped by the
+// tensor store); otherwise rows past M return early.
 __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long long orow, float* v, bool row_ok,
-                                         const Chunk32& c) {
+                                         const Chunk32& c, const CUtensorMap* tmC, EpiStore& es, int lane) {
   if (ep.bias != nullptr) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -121,6 +181,22 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
   if (ep.act == VLA_ACT_GELU_TANH) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
+  }
+  if (ep.tma_c) {  // never Euler: the residual follows bias / GELU directly
+    if (ep.residual != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float r[8];
+        unpack_bf16x8(c.r[i], r);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[8 * i + e] += r[e];
+      }
+    }
+    uint4 pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x8(v + 8 * i);
+    stage_store<4>(tmC, es, pk, lane, n);
+    return;
   }
   if (!row_ok) return;
   const int nv = chunk_vecs(ep, n);
@@ -245,7 +321,7 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
 // lane quarter split the column chunks round-robin (part of nparts).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, int part,
-                                              int nparts) {
+                                              int nparts, const CUtensorMap* tmC, EpiStore& es, int lane) {
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
@@ -257,17 +333,23 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       tmem_ld16(taddr + c, g);
       tmem_ld16(taddr + c + 16, u);
       const int n = n0 + c;
-      if (n >= ep.N || !row_ok) continue;
+      if (n >= ep.N) break;
+      if (!row_ok && !ep.tma_c) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * ep.alpha) * (u[i] * ep.alpha);
       const int nc = n >> 1;
-      if (ep.residual != nullptr) {
+      if (ep.residual != nullptr && row_ok) {
         const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + nc);
         float r[16];
         unpack_bf16x8(rp[0], r);
         unpack_bf16x8(rp[1], r + 8);
 #pragma unroll
         for (int i = 0; i < 16; ++i) g[i] += r[i];
+      }
+      if (ep.tma_c) {
+        const uint4 pk[2] = {pack_bf16x8(g), pack_bf16x8(g + 8)};
+        stage_store<2>(tmC, es, pk, lane, nc);
+        continue;
       }
       uint4* cp = reinterpret_cast<uint4*>(ep.C + orow * ep.ldc + nc);
       cp[0] = pack_bf16x8(g);
@@ -291,7 +373,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       if (more) prefetch32(ep, m, n + step, row_ok, nxt);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
-      finish32(ep, m, n, orow, v, row_ok, cur);
+      finish32(ep, m, n, orow, v, row_ok, cur, tmC, es, lane);
       if (more) cur = nxt;
     }
   }
@@ -299,15 +381,16 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, DevEpi ep,
-                        int M, int N, int K) {
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, DevEpi ep, int M, int N, int K) {
   using Cf = Cfg<BN>;
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * Cf::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cf::B_BYTES);
+  uint8_t* sC = sB + STAGES * Cf::B_BYTES;  // output staging (1024-byte aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + kEpiStoreBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -334,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (ep.tma_c) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cf::TMEM_COLS);
   tc_fence_before();
@@ -415,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;               // TMEM lane quarter this warp may access
     const int part = (warp - 2) >> 2;     // which column share of that quarter
+    EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0};
     int tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mb, nb;
@@ -432,12 +517,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int m = mb * BM + q * 32 + lane;
+      es.row0 = mb * BM + q * 32;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, es, lane);
       tc_fence_before();
       mbar_arrive(&tempty[as]);
       ++tc;
     }
+    if (ep.tma_c) stage_drain(lane);
   }
   tc_fence_before();
   __syncthreads();

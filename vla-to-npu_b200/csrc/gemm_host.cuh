@@ -57,8 +57,8 @@ static int max_pair_clusters() {
 }
 
 template <int BN>
-static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const DevEpi& ep, int64_t M, int64_t N,
-                      int64_t K, cudaStream_t st) {
+static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const DevEpi& ep,
+                      int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   using Cf = Cfg2<BN>;
   CUtensorMap tb;
   int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN / 2);
@@ -76,7 +76,7 @@ static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const D
   const int clusters = max_pair_clusters<BN>();
   const int grid = 2 * (int)(tiles < clusters ? tiles : clusters);
   prof_begin(st);
-  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ep, (int)M,
+  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, ep, (int)M,
                    (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -98,8 +98,8 @@ static int choose_ctas(int64_t M, int bn) {
 }
 
 template <int BN>
-static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const DevEpi& ep, int64_t M, int64_t N,
-                     int64_t K, cudaStream_t st) {
+static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const DevEpi& ep,
+                     int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   using Cf = Cfg<BN>;
   CUtensorMap tb;
   int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
@@ -116,7 +116,8 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const De
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
   prof_begin(st);
-  launch_k(gemm_bf16_tc_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ep, (int)M, (int)N, (int)K);
+  launch_k(gemm_bf16_tc_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, ep, (int)M, (int)N,
+           (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
@@ -188,6 +189,19 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   CUtensorMap ta;
   int rc = make_tmap_bf16_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
   if (rc) return rc;
+  // Output through shared memory + TMA stores for the plain / bias / GELU /
+  // residual / SwiGLU epilogues (row scatter, RoPE and Euler store directly).
+  // Box: 32 rows x 32 columns (64-byte swizzle), or 16 columns for SwiGLU's
+  // halved output (32-byte swizzle); out-of-range rows and columns are clipped.
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof(tc));
+  ep.tma_c = (act == VLA_ACT_NONE || act == VLA_ACT_GELU_TANH || act == VLA_ACT_SWIGLU) && ep.out_grp == 0;
+  if (ep.tma_c) {
+    const bool sw = act == VLA_ACT_SWIGLU;
+    rc = make_tmap_bf16_2d(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)ldc, sw ? 16u : 32u, 32u,
+                           sw ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
   const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
   // VLA_GEMM_CTAS=1|2 overrides the automatic one-CTA / pair choice (A/B measurement)
   static const int env_ctas = [] {
@@ -200,25 +214,25 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
   if (ctas == 2) {
     switch (bn) {
-      case 256: return launch_bn2<256>(ta, B, ldb, ep, M, N, K, st);
-      case 224: return launch_bn2<224>(ta, B, ldb, ep, M, N, K, st);
-      case 192: return launch_bn2<192>(ta, B, ldb, ep, M, N, K, st);
-      case 160: return launch_bn2<160>(ta, B, ldb, ep, M, N, K, st);
-      case 128: return launch_bn2<128>(ta, B, ldb, ep, M, N, K, st);
-      case 96: return launch_bn2<96>(ta, B, ldb, ep, M, N, K, st);
-      case 64: return launch_bn2<64>(ta, B, ldb, ep, M, N, K, st);
+      case 256: return launch_bn2<256>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 224: return launch_bn2<224>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 192: return launch_bn2<192>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 160: return launch_bn2<160>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 128: return launch_bn2<128>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 96: return launch_bn2<96>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 64: return launch_bn2<64>(ta, B, ldb, tc, ep, M, N, K, st);
       default: return set_error(VLA_E_UNSUPPORTED, "gemm: pair tile width %d not built", bn);
     }
   }
   switch (bn) {
-    case 256: return launch_bn<256>(ta, B, ldb, ep, M, N, K, st);
-    case 224: return launch_bn<224>(ta, B, ldb, ep, M, N, K, st);
-    case 192: return launch_bn<192>(ta, B, ldb, ep, M, N, K, st);
-    case 160: return launch_bn<160>(ta, B, ldb, ep, M, N, K, st);
-    case 128: return launch_bn<128>(ta, B, ldb, ep, M, N, K, st);
-    case 96: return launch_bn<96>(ta, B, ldb, ep, M, N, K, st);
-    case 64: return launch_bn<64>(ta, B, ldb, ep, M, N, K, st);
-    case 32: return launch_bn<32>(ta, B, ldb, ep, M, N, K, st);
+    case 256: return launch_bn<256>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 224: return launch_bn<224>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 192: return launch_bn<192>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 160: return launch_bn<160>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 128: return launch_bn<128>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 96: return launch_bn<96>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 64: return launch_bn<64>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 32: return launch_bn<32>(ta, B, ldb, tc, ep, M, N, K, st);
     default: return set_error(VLA_E_UNSUPPORTED, "gemm: tile width %d not built", bn);
   }
 }

@@ -81,7 +81,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 // ld (elements); box = [box_outer rows, box_inner cols]; 128-byte swizzle.
 // Out-of-range boxes are zero-filled by the TMA unit.
 static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
-                             uint32_t box_inner, uint32_t box_outer) {
+                             uint32_t box_inner, uint32_t box_outer,
+                             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = tmap_encoder();
   if (enc == nullptr) return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t dims[2] = {inner, outer};
@@ -89,7 +90,7 @@ static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, ui
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu box=%ux%u", (int)r,
