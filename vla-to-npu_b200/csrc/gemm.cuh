@@ -50,6 +50,7 @@ struct DevEpi {
   long long ldx;
   float euler_dt;
   int tma_c;  // stores go through shared memory and the C tensor map
+  int tma_r;  // the residual arrives in the same staging buffers through its tensor map
   int M, N;
 };
 
@@ -58,12 +59,36 @@ struct DevEpi {
 constexpr int kStageC = 32 * 64;
 constexpr int kEpiStoreBytes = kEpiWarps * 2 * kStageC;
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per block on sm_100
+constexpr int kBarrierBytes = 512;  // mbarriers, TMEM slot and abort flag
 
 struct EpiStore {
-  uint32_t buf;  // shared address of this warp's two staging buffers
-  int sb;        // buffer the next chunk uses
-  int row0;      // output row of the warp's lane 0
+  uint32_t buf;   // shared address of this warp's two staging buffers
+  int sb;         // buffer the next chunk uses
+  int row0;       // output row of the warp's lane 0
+  uint64_t* rbar; // two barriers: residual chunk landed in buffer 0 / 1
+  uint32_t rpar;  // bit b: phase parity of the next residual arrival in buffer b
+  volatile int* abort_flag;
 };
+
+// Issue the TMA load of the residual chunk at (col, res_row) into staging
+// buffer `b` (lane 0).  `pending_ok` stores may still be reading staging
+// buffers: 1 when `b` is the buffer used two chunks ago, 0 when it is the one
+// the previous chunk used.
+__device__ __forceinline__ void res_load(const CUtensorMap* tmR, EpiStore& es, int b, int col, int res_row,
+                                         int pending_ok, int lane) {
+  if (lane == 0) {
+    if (pending_ok)
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    else
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    mbar_arrive_expect_tx(&es.rbar[b], (uint32_t)kStageC);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            es.buf + (uint32_t)b * (uint32_t)kStageC),
+        "l"(reinterpret_cast<uint64_t>(tmR)), "r"(col), "r"(res_row), "r"(smem_u32(&es.rbar[b]))
+        : "memory");
+  }
+}
 
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t smem, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -98,6 +123,36 @@ __device__ __forceinline__ void stage_store(const CUtensorMap* tm, EpiStore& es,
   es.sb ^= 1;
 }
 
+// Stage-and-store with the residual already in the staging buffer: this lane's
+// row is read from shared memory, added to v, and the sum stored in place.
+__device__ __forceinline__ void res_stage_store(const CUtensorMap* tmC, EpiStore& es, float* v, int lane, int col) {
+  const uint32_t b = es.buf + (uint32_t)es.sb * (uint32_t)kStageC;
+  const bool ok = mbar_wait_bounded(&es.rbar[es.sb], (es.rpar >> es.sb) & 1u, es.abort_flag);
+  es.rpar ^= 1u << es.sb;
+  if (!ok && lane == 0) {  // the result is not valid; the error word says so
+    if (!*es.abort_flag) vla_record_error(VLA_DERR_GEMM_EPILOGUE_TIMEOUT);
+    *es.abort_flag = 1;
+  }
+  uint4 pk[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t a = b + (uint32_t)(lane * 64 + ((i ^ ((lane >> 1) & 3)) * 16));
+    uint4 r;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    float rf[8];
+    unpack_bf16x8(r, rf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[8 * i + e] += rf[e];
+    pk[i] = pack_bf16x8(v + 8 * i);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) st_shared_v4(b + (uint32_t)(lane * 64 + ((i ^ ((lane >> 1) & 3)) * 16)), pk[i]);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) tma_store_2d(tmC, b, col, es.row0);
+  es.sb ^= 1;
+}
+
 // All of this warp's TMA stores have completed (issued by lane 0).
 __device__ __forceinline__ void stage_drain(int lane) {
   if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -109,10 +164,10 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BUDGET = kSmemLimit - 1024 - 256 - kEpiStoreBytes;
+  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + 256 + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (multiple of 32 for the epilogue chunks)");
   static_assert(B_BYTES % 1024 == 0, "B tile alignment");
 };
@@ -150,7 +205,7 @@ __device__ __forceinline__ void prefetch32(const DevEpi& ep, int m, int n, bool 
   const int nv = chunk_vecs(ep, n);
 #pragma unroll
   for (int i = 0; i < 4; ++i) c.r[i] = c.b[i] = make_uint4(0u, 0u, 0u, 0u);
-  if (ep.residual != nullptr && row_ok) {
+  if (ep.residual != nullptr && row_ok && !ep.tma_r) {
     const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + n);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -183,6 +238,10 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
     for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
   }
   if (ep.tma_c) {  // never Euler: the residual follows bias / GELU directly
+    if (ep.tma_r) {
+      res_stage_store(tmC, es, v, lane, n);
+      return;
+    }
     if (ep.residual != nullptr) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -321,7 +380,8 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
 // lane quarter split the column chunks round-robin (part of nparts).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, int part,
-                                              int nparts, const CUtensorMap* tmC, EpiStore& es, int lane) {
+                                              int nparts, const CUtensorMap* tmC, const CUtensorMap* tmR,
+                                              EpiStore& es, int lane) {
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
@@ -361,7 +421,13 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
     const int step = 32 * nparts;
     int c = 32 * part;
     Chunk32 cur, nxt;
-    if (c < BN && n0 + c < ep.N) prefetch32(ep, m, n0 + c, row_ok, cur);
+    // residual rows of this warp's 32 output rows (blocks of 32 never straddle
+    // the res_row_mod period: the host only sets tma_r when it divides by 32)
+    const int rrow = (int)res_row(ep, es.row0);
+    if (c < BN && n0 + c < ep.N) {
+      prefetch32(ep, m, n0 + c, row_ok, cur);
+      if (ep.tma_r) res_load(tmR, es, es.sb, n0 + c, rrow, 1, lane);
+    }
 #pragma unroll 1
     for (; c < BN; c += step) {
       const int n = n0 + c;
@@ -370,7 +436,10 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       tmem_ld16(taddr + c, v);
       tmem_ld16(taddr + c + 16, v + 16);
       const bool more = c + step < BN && n + step < ep.N;
-      if (more) prefetch32(ep, m, n + step, row_ok, nxt);
+      if (more) {
+        prefetch32(ep, m, n + step, row_ok, nxt);
+        if (ep.tma_r) res_load(tmR, es, es.sb ^ 1, n + step, rrow, 0, lane);
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
       finish32(ep, m, n, orow, v, row_ok, cur, tmC, es, lane);
@@ -382,7 +451,8 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, DevEpi ep, int M, int N, int K) {
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
+                        int M, int N, int K) {
   using Cf = Cfg<BN>;
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -394,7 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // [kEpiWarps][2]: residual chunk landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -413,11 +484,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 32 * kEpiWarps);
     }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
     *abort_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (ep.tma_c) tma_prefetch_desc(&tmC);
+    if (ep.tma_r) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cf::TMEM_COLS);
   tc_fence_before();
@@ -499,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;               // TMEM lane quarter this warp may access
     const int part = (warp - 2) >> 2;     // which column share of that quarter
-    EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0};
+    EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0, rbar + 2 * (warp - 2), 0u, abort_flag};
     int tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mb, nb;
@@ -519,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = mb * BM + q * 32 + lane;
       es.row0 = mb * BM + q * 32;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, es, lane);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
       tc_fence_before();
       mbar_arrive(&tempty[as]);
       ++tc;

@@ -24,10 +24,10 @@ struct Cfg2 {
   static constexpr int A_BYTES = BM * BK * 2;        // 128 rows of A per CTA
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // half of the B tile per CTA
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BUDGET = kSmemLimit - 1024 - 256 - kEpiStoreBytes;
+  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + 256 + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "UMMA N");
   static_assert(B_BYTES % 1024 == 0, "B half-tile alignment (BN/2 multiple of 8)");
 };
@@ -96,7 +96,8 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmC, DevEpi ep, int M, int N, int K) {
+                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
+                         int M, int N, int K) {
   using Cf = Cfg2<BN>;
   constexpr int STAGES = Cf::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -108,7 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // [kEpiWarps][2]: residual chunk landed (this CTA's)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -131,10 +133,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs (leader's copy)
     }
     *abort_flag = 0;
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (ep.tma_c) tma_prefetch_desc(&tmC);
+    if (ep.tma_r) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int part = (warp - 2) >> 2;
     const uint32_t leader_tempty0 = map_to_rank(smem_u32(&tempty[0]), 0);
     const uint32_t leader_tempty1 = map_to_rank(smem_u32(&tempty[1]), 0);
-    EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0};
+    EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0, rbar + 2 * (warp - 2), 0u, abort_flag};
     int tc = 0;
     for (int t = cluster; t < num_tiles; t += n_clusters) {
       int mb, nb;
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = mb * 2 * BM + (int)rank * BM + q * 32 + lane;
       es.row0 = mb * 2 * BM + (int)rank * BM + q * 32;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, es, lane);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster_relaxed(as ? leader_tempty1 : leader_tempty0);

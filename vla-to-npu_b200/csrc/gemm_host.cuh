@@ -57,7 +57,8 @@ static int max_pair_clusters() {
 }
 
 template <int BN>
-static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const DevEpi& ep,
+static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const CUtensorMap& tr,
+                      const DevEpi& ep,
                       int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   using Cf = Cfg2<BN>;
   CUtensorMap tb;
@@ -76,7 +77,7 @@ static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const C
   const int clusters = max_pair_clusters<BN>();
   const int grid = 2 * (int)(tiles < clusters ? tiles : clusters);
   prof_begin(st);
-  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, ep, (int)M,
+  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, tr, ep, (int)M,
                    (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -98,7 +99,8 @@ static int choose_ctas(int64_t M, int bn) {
 }
 
 template <int BN>
-static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const DevEpi& ep,
+static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const CUtensorMap& tr,
+                     const DevEpi& ep,
                      int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   using Cf = Cfg<BN>;
   CUtensorMap tb;
@@ -116,7 +118,7 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CU
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
   prof_begin(st);
-  launch_k(gemm_bf16_tc_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, ep, (int)M, (int)N,
+  launch_k(gemm_bf16_tc_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, tr, ep, (int)M, (int)N,
            (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -202,6 +204,18 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                            sw ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   }
+  // The residual through the same staging buffers (32 x 32 chunks, 64-byte
+  // swizzle) when each 32-row block maps to 32 consecutive residual rows.
+  CUtensorMap tr;
+  memset(&tr, 0, sizeof(tr));
+  ep.tma_r = ep.tma_c && ep.residual != nullptr && act != VLA_ACT_SWIGLU &&
+             (ep.res_row_mod == 0 || ep.res_row_mod % 32 == 0);
+  if (ep.tma_r) {
+    const uint64_t rows = ep.res_row_mod > 0 ? (uint64_t)ep.res_row_mod : (uint64_t)M;
+    rc = make_tmap_bf16_2d(&tr, ep.residual, (uint64_t)out_cols, rows, (uint64_t)ep.ldr, 32u, 32u,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
   const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
   // VLA_GEMM_CTAS=1|2 overrides the automatic one-CTA / pair choice (A/B measurement)
   static const int env_ctas = [] {
@@ -214,25 +228,25 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
   if (ctas == 2) {
     switch (bn) {
-      case 256: return launch_bn2<256>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 224: return launch_bn2<224>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 192: return launch_bn2<192>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 160: return launch_bn2<160>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 128: return launch_bn2<128>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 96: return launch_bn2<96>(ta, B, ldb, tc, ep, M, N, K, st);
-      case 64: return launch_bn2<64>(ta, B, ldb, tc, ep, M, N, K, st);
+      case 256: return launch_bn2<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 224: return launch_bn2<224>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 192: return launch_bn2<192>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 160: return launch_bn2<160>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 128: return launch_bn2<128>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 96: return launch_bn2<96>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 64: return launch_bn2<64>(ta, B, ldb, tc, tr, ep, M, N, K, st);
       default: return set_error(VLA_E_UNSUPPORTED, "gemm: pair tile width %d not built", bn);
     }
   }
   switch (bn) {
-    case 256: return launch_bn<256>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 224: return launch_bn<224>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 192: return launch_bn<192>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 160: return launch_bn<160>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 128: return launch_bn<128>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 96: return launch_bn<96>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 64: return launch_bn<64>(ta, B, ldb, tc, ep, M, N, K, st);
-    case 32: return launch_bn<32>(ta, B, ldb, tc, ep, M, N, K, st);
+    case 256: return launch_bn<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 224: return launch_bn<224>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 192: return launch_bn<192>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 160: return launch_bn<160>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 128: return launch_bn<128>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 96: return launch_bn<96>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 64: return launch_bn<64>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+    case 32: return launch_bn<32>(ta, B, ldb, tc, tr, ep, M, N, K, st);
     default: return set_error(VLA_E_UNSUPPORTED, "gemm: tile width %d not built", bn);
   }
 }
