@@ -13,7 +13,7 @@
 //               of 32 rows x 32 columns go through a per-warp shared-memory
 //               staging buffer and a TMA tensor store (full-line global writes;
 //               direct per-row stores touch 32 lines per warp instruction and
-//               made the epilogue the bound of short-K GEMMs); RoPE, Euler and
+//               made the epilogue the bound of short-K GEMMs); Euler and
 //               row-scatter epilogues store directly.
 //
 // This is the replacement for the reference's Allo GEMM module plus the host
@@ -300,7 +300,8 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
 // GEMMs bound by L1 wavefronts).
 template <int BN>
 __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, long long orow,
-                                          bool row_ok, int part, int nparts) {
+                                          bool row_ok, int part, int nparts, const CUtensorMap* tmC, EpiStore& es,
+                                          int lane) {
   const bool split = (nparts & 1) == 0;
   const int hq0 = split ? (part & 1) : 0;
   const int hq1 = split ? (part & 1) : 1;
@@ -317,13 +318,13 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
       if (n >= ep.N) break;
       float lo[16], hi[16];
       tmem_ld16x2(taddr + 64 * h + 16 * hq, taddr + 64 * h + 32 + 16 * hq, lo, hi);
-      if (!row_ok) continue;
+      if (!row_ok && !ep.tma_c) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         lo[i] *= ep.alpha;
         hi[i] *= ep.alpha;
       }
-      if (ep.bias != nullptr) {
+      if (ep.bias != nullptr) {  // the same address on every lane: one broadcast load
         float b[8];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -353,6 +354,13 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
           lo[e] = a * cc[e] - b * ss[e];
           hi[e] = b * cc[e] + a * ss[e];
         }
+      }
+      if (ep.tma_c) {  // (no residual: the host sends RoPE + residual down the direct path)
+        const uint4 plo[2] = {pack_bf16x8(lo), pack_bf16x8(lo + 8)};
+        const uint4 phi[2] = {pack_bf16x8(hi), pack_bf16x8(hi + 8)};
+        stage_store<2>(tmC, es, plo, lane, n + 16 * hq);
+        stage_store<2>(tmC, es, phi, lane, n + 32 + 16 * hq);
+        continue;
       }
       if (ep.residual != nullptr) {
         const bf16* rp = ep.residual + res_row(ep, m) * ep.ldr + n;
@@ -385,7 +393,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
-    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts);
+    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts, tmC, es, lane);
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
     for (int c = 32 * part; c < BN; c += 32 * nparts) {

@@ -192,14 +192,17 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   int rc = make_tmap_bf16_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
   if (rc) return rc;
   // Output through shared memory + TMA stores for the plain / bias / GELU /
-  // residual / SwiGLU epilogues (row scatter, RoPE and Euler store directly).
-  // Box: 32 rows x 32 columns (64-byte swizzle), or 16 columns for SwiGLU's
-  // halved output (32-byte swizzle); out-of-range rows and columns are clipped.
+  // residual / SwiGLU / RoPE epilogues (row scatter and Euler store directly).
+  // Box: 32 rows x 32 columns (64-byte swizzle), or 16 columns (32-byte
+  // swizzle); out-of-range rows and columns are clipped.
   CUtensorMap tc;
   memset(&tc, 0, sizeof(tc));
-  ep.tma_c = (act == VLA_ACT_NONE || act == VLA_ACT_GELU_TANH || act == VLA_ACT_SWIGLU) && ep.out_grp == 0;
+  ep.tma_c = (act == VLA_ACT_NONE || act == VLA_ACT_GELU_TANH || act == VLA_ACT_SWIGLU ||
+              (act == VLA_ACT_ROPE && ep.residual == nullptr)) &&
+             ep.out_grp == 0;
   if (ep.tma_c) {
-    const bool sw = act == VLA_ACT_SWIGLU;
+    // 16-column boxes for SwiGLU's halved output and for RoPE's half-head segments
+    const bool sw = act == VLA_ACT_SWIGLU || act == VLA_ACT_ROPE;
     rc = make_tmap_bf16_2d(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)ldc, sw ? 16u : 32u, 32u,
                            sw ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
