@@ -84,7 +84,7 @@ __device__ __forceinline__ void load_tile(bf16* s, const bf16* g, long long row_
   }
 }
 
-__global__ void __launch_bounds__(kThreads) flash_attn_kernel(Params p) {
+__global__ void __launch_bounds__(kThreads, 4) flash_attn_kernel(Params p) {
   pdl_prologue();
   __shared__ __align__(128) bf16 sQ[BQ * HD];
   __shared__ __align__(128) bf16 sK[2][BKV * HD];
