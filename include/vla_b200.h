@@ -76,18 +76,8 @@ typedef struct vla_epilogue {
   float* euler_x;        /* fp32 [M, ldx] Euler state (VLA_ACT_EULER) */
   int64_t ldx;
   float euler_dt;
-  /* Normalisation of the A rows folded into the GEMM (the GEMM reads the raw
-   * rows; B must carry the norm's gain, B[n, k] = W[n, k] * g[k]):
-   *   VLA_NORM_RMS: C = epi(rstd_m * acc),  rstd_m = 1 / sqrt(mean_k A[m,k]^2 + eps)
-   *   VLA_NORM_LN:  C = epi(rstd_m * (acc - mu_m * norm_colsum[n])), mu / rstd the
-   *                 row mean / inverse std of A; norm_colsum[n] = sum_k B[n, k]
-   *                 (fp32) and the LayerNorm shift enters through `bias`
-   *                 (b[n] + sum_k beta[k] W[n, k]).  Not with VLA_ACT_EULER. */
-  int32_t norm;              /* VLA_NORM_NONE / _RMS / _LN */
-  float norm_eps;
-  const float* norm_colsum;  /* fp32 [N] (VLA_NORM_LN) */
+  int32_t reserved[4];
 } vla_epilogue;
-enum { VLA_NORM_NONE = 0, VLA_NORM_RMS = 1, VLA_NORM_LN = 2 };
 
 /* ---------------------------------------------------------------------- */
 /* Library status                                                          */

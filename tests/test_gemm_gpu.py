@@ -141,72 +141,3 @@ def test_gemm_rope_tile_widths(cuda, tile_n, ctas):
     ref = torch.cat([rot, y[:, nrot:]], 1) + r.float()
     torch.testing.assert_close(out.float().cpu(), ref, atol=4e-2, rtol=2e-2)
     dev.sync_check()
-
-
-@pytest.mark.gpu
-@pytest.mark.parametrize("ctas", [1, 2])
-@pytest.mark.parametrize("K", [720, 768])
-def test_gemm_folded_norms(cuda, ctas, K):
-    """RMSNorm / LayerNorm of the A rows folded into the GEMM (gain folded into
-    B, row statistics from the kernel's statistics warps) against fp32 torch
-    norm-then-GEMM, for the plain, SwiGLU, RoPE, bias+GELU and residual epilogues."""
-    import torch.nn.functional as F
-    from oracle import smolvla_ref as R
-    from vla_b200 import _lib, device as dev
-    from vla_b200.model import interleave_gate_up, rope_table
-    g = torch.Generator().manual_seed(41)
-    M, eps = 4200 if ctas == 2 else 700, 1e-5
-    x = (torch.randn(M, K, generator=g) * 1.5 + 0.3).to(torch.bfloat16)
-    gam = (1.0 + 0.2 * torch.randn(K, generator=g)).to(torch.bfloat16)
-    xc = x.cuda()
-
-    def rms(t):
-        t = t.float()
-        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps) * gam.float()
-
-    def fold(w):  # [N, K] * gain over K
-        return (w.float() * gam.float()).to(torch.bfloat16)
-
-    # RMS, plain
-    w = (torch.randn(320, K, generator=g) * 0.05).to(torch.bfloat16)
-    out = torch.empty(M, 320, dtype=torch.bfloat16, device="cuda")
-    dev.gemm(xc, fold(w).cuda(), out, dev.make_epilogue(norm=_lib.NORM_RMS, norm_eps=eps), ctas=ctas)
-    torch.testing.assert_close(out.float().cpu(), rms(x) @ w.float().T, atol=3e-2, rtol=2e-2)
-    # RMS, SwiGLU
-    wg, wu = (torch.randn(K, 256, generator=g) * 0.05).to(torch.bfloat16), \
-        (torch.randn(K, 256, generator=g) * 0.05).to(torch.bfloat16)
-    wgu = interleave_gate_up((wg.float() * gam.float()[:, None]).to(torch.bfloat16),
-                             (wu.float() * gam.float()[:, None]).to(torch.bfloat16), "cuda")
-    out = torch.empty(M, 256, dtype=torch.bfloat16, device="cuda")
-    dev.gemm(xc, wgu, out, dev.make_epilogue(act=_lib.ACT_SWIGLU, norm=_lib.NORM_RMS, norm_eps=eps), ctas=ctas)
-    h = rms(x)
-    torch.testing.assert_close(out.float().cpu(), F.silu(h @ wg.float()) * (h @ wu.float()), atol=3e-2, rtol=2e-2)
-    # RMS, RoPE on the first 2 of 3 heads
-    wq = (torch.randn(192, K, generator=g) * 0.05).to(torch.bfloat16)
-    cs = rope_table(50, 64, 1e4).cuda()
-    out = torch.empty(M, 192, dtype=torch.bfloat16, device="cuda")
-    dev.gemm(xc, fold(wq).cuda(), out, dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=128,
-                                                         norm=_lib.NORM_RMS, norm_eps=eps), ctas=ctas)
-    y = h @ wq.float().T
-    pos = (torch.arange(M) % 50).float()
-    rot = R.apply_rope(y[:, :128].reshape(M, 1, 2, 64), 1e4, positions=pos[:, None]).reshape(M, 128)
-    torch.testing.assert_close(out.float().cpu(), torch.cat([rot, y[:, 128:]], 1), atol=3e-2, rtol=2e-2)
-    # LayerNorm, bias + GELU; then LayerNorm + residual
-    beta = (0.1 * torch.randn(K, generator=g)).to(torch.bfloat16)
-    b = (0.1 * torch.randn(384, generator=g)).to(torch.bfloat16)
-    w = (torch.randn(384, K, generator=g) * 0.05).to(torch.bfloat16)
-    wf = fold(w)
-    colsum = wf.float().sum(1).cuda()
-    bias2 = (b.float() + beta.float() @ w.float().T).to(torch.bfloat16).cuda()
-    ln = F.layer_norm(x.float(), (K,), gam.float(), beta.float(), eps)
-    out = torch.empty(M, 384, dtype=torch.bfloat16, device="cuda")
-    dev.gemm(xc, wf.cuda(), out, dev.make_epilogue(bias=bias2, act=_lib.ACT_GELU_TANH, norm=_lib.NORM_LN,
-                                                    norm_eps=eps, norm_colsum=colsum), ctas=ctas)
-    ref = F.gelu(ln @ w.float().T + b.float(), approximate="tanh")
-    torch.testing.assert_close(out.float().cpu(), ref, atol=3e-2, rtol=2e-2)
-    res = torch.randn(M, 384, generator=g).to(torch.bfloat16)
-    out = res.cuda().clone()
-    dev.gemm(xc, wf.cuda(), out, dev.make_epilogue(bias=bias2, residual=out, norm=_lib.NORM_LN, norm_eps=eps,
-                                                    norm_colsum=colsum), ctas=ctas)
-    torch.testing.assert_close(out.float().cpu(), ln @ w.float().T + b.float() + res.float(), atol=4e-2, rtol=2e-2)
-    dev.sync_check()

@@ -105,30 +105,6 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait on the phase with the given parity.  Returns false when the
 // time limit expires or when another role of the CTA raised *abort.
-// Bounded wait with cluster-scope acquire: for a phase completed by another
-// CTA of the cluster (a remote arrive with release.cluster).
-__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                          uint64_t limit_ns = VLA_WAIT_LIMIT_NS) {
-  const uint32_t a = smem_u32(bar);
-  uint64_t t0 = 0;
-  for (uint32_t i = 0;; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (i == 0) t0 = vla_globaltimer();
-    if ((i & 255u) == 255u) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (vla_globaltimer() - t0 > limit_ns) return false;
-    }
-  }
-}
-
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                   uint64_t limit_ns = VLA_WAIT_LIMIT_NS) {
   const uint32_t a = smem_u32(bar);

@@ -29,8 +29,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter, splitting the columns
-constexpr int kStatWarps = 2;                // per-row statistics of the A tiles (folded norms)
-constexpr int kThreads = 64 + 32 * kEpiWarps + 32 * kStatWarps;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-blocks sweep all N-blocks
 
 struct DevEpi {
@@ -52,10 +51,6 @@ struct DevEpi {
   float euler_dt;
   int tma_c;  // stores go through shared memory and the C tensor map
   int tma_r;  // the residual arrives in the same staging buffers through its tensor map
-  int norm;   // VLA_NORM_*: row statistics of A from the statistics warps
-  float norm_eps;
-  const float* norm_colsum;
-  int K;
   int M, N;
 };
 
@@ -64,108 +59,7 @@ struct DevEpi {
 constexpr int kStageC = 32 * 64;
 constexpr int kEpiStoreBytes = kEpiWarps * 2 * kStageC;
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per block on sm_100
-constexpr int kBarrierBytes = 384;  // mbarriers (<= 46), TMEM slot and abort flag
-// (mean, rstd) of the tile's 128 rows, single-buffered: the epilogue reads tile
-// t's at the start of its epilogue, the statistics warps write tile t+1's only
-// after that (they wait for the epilogue's release before writing).
-constexpr int kNormBytes = BM * 8;
-
-// Row statistics of one 128-row A stage (128-byte rows, swizzled in 16-byte
-// chunks within the row, so a row's 64 values are the 128 bytes at r * 128):
-// this lane adds rows r0 and r0 + 32 to (sum, sum of squares).  Columns past K
-// were zero-filled by TMA and add nothing.
-__device__ __forceinline__ void row_stats_stage(uint32_t a_stage, int r0, float* s, float* q) {
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const uint32_t row = a_stage + (uint32_t)((r0 + 32 * rr) * 128);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 u;
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
-                   : "r"(row + 16u * c));
-      float f[8];
-      unpack_bf16x8(u, f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        s[rr] += f[e];
-        q[rr] = fmaf(f[e], f[e], q[rr]);
-      }
-    }
-  }
-}
-
-// (mean, rstd) of a row from its sums over K columns (fp32, as the separate
-// norm kernels compute them).
-__device__ __forceinline__ float2 row_norm(const DevEpi& ep, float s, float q) {
-  const float inv_k = 1.f / (float)ep.K;
-  if (ep.norm == VLA_NORM_RMS) return make_float2(0.f, rsqrtf(q * inv_k + ep.norm_eps));
-  const float mu = s * inv_k;
-  const float var = fmaxf(q * inv_k - mu * mu, 0.f);
-  return make_float2(mu, rsqrtf(var + ep.norm_eps));
-}
-
-// The statistics warps of a GEMM with a folded norm: for each of this CTA's
-// tiles, walk its k-blocks in step with the MMA (stage `it` is ready on
-// ready[it % stages]; with `cluster_ready` the phase was completed by the
-// pair's leader), add this lane's rows r0, r0 + 32 of the A stage to the row
-// sums, release the stage on empty[], and at the tile's end publish the rows'
-// (mean, rstd) to the epilogue.  A non-zero `relay` (shared::cluster address
-// of the other CTA's ready[0]) forwards each stage's arrival there.  Returns
-// false on a timeout.
-__device__ __forceinline__ bool stat_warps(const DevEpi& ep, uint8_t* sA, int a_bytes, int stages, uint64_t* ready,
-                                           bool cluster_ready, uint64_t* empty, float2* nstat, uint64_t* nfull,
-                                           uint64_t* nempty, volatile int* abort_flag, int first_tile,
-                                           int tile_step, int num_tiles, int num_kb, int r0, int lane,
-                                           uint32_t relay = 0u) {
-  int it = 0, tc = 0;
-  bool ok = true;
-  for (int t = first_tile; t < num_tiles && ok; t += tile_step) {
-    float s[2] = {0.f, 0.f}, q[2] = {0.f, 0.f};
-    for (int kb = 0; kb < num_kb && ok; ++kb) {
-      const int st = it % stages;
-      const uint32_t ph = (uint32_t)(it / stages) & 1u;
-      ok = cluster_ready ? mbar_wait_bounded_cluster(&ready[st], ph, abort_flag)
-                         : mbar_wait_bounded(&ready[st], ph, abort_flag);
-      if (!ok) break;
-      if (relay != 0u && lane == 0) {  // stage st landed: tell the pair's other CTA (shared::cluster address)
-        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(relay + 8u * (uint32_t)st)
-                     : "memory");
-      }
-      row_stats_stage(smem_u32(sA + st * a_bytes), r0, s, q);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      ++it;
-    }
-    // the single (mean, rstd) buffer is free once the epilogue read the previous tile's
-    if (ok) ok = mbar_wait_bounded(nempty, ((uint32_t)tc & 1u) ^ 1u, abort_flag);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok) break;
-    nstat[r0] = row_norm(ep, s[0], q[0]);
-    nstat[r0 + 32] = row_norm(ep, s[1], q[1]);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(nfull);
-    ++tc;
-  }
-  return ok;
-}
-
-// Epilogue side of the folded norm: this lane's row scale (alpha * rstd) and
-// shift (alpha * rstd * mean) for tile number tc of this CTA.
-__device__ __forceinline__ bool norm_row_scale(const DevEpi& ep, float2* nstat, uint64_t* nfull, uint64_t* nempty,
-                                               volatile int* abort_flag, int tc, int row, int lane, float& alpha,
-                                               float& amu) {
-  alpha = ep.alpha;
-  amu = 0.f;
-  if (!ep.norm) return true;
-  const bool ok = mbar_wait_bounded(nfull, (uint32_t)tc & 1u, abort_flag);
-  const float2 st = nstat[row];
-  alpha *= st.y;
-  amu = alpha * st.x;
-  __syncwarp();
-  if (lane == 0) mbar_arrive(nempty);
-  return __all_sync(0xffffffffu, ok);
-}
+constexpr int kBarrierBytes = 512;  // mbarriers, TMEM slot and abort flag
 
 struct EpiStore {
   uint32_t buf;   // shared address of this warp's two staging buffers
@@ -270,13 +164,12 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes - kNormBytes;
+  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kNormBytes + kBarrierBytes + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N (multiple of 32 for the epilogue chunks)");
   static_assert(B_BYTES % 1024 == 0, "B tile alignment");
-  static_assert((2 * STAGES + 4 + 2 * kEpiWarps + 2) * 8 + 8 <= kBarrierBytes, "barrier area");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -408,7 +301,7 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
 template <int BN>
 __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, long long orow,
                                           bool row_ok, int part, int nparts, const CUtensorMap* tmC, EpiStore& es,
-                                          int lane, float alpha) {
+                                          int lane) {
   const bool split = (nparts & 1) == 0;
   const int hq0 = split ? (part & 1) : 0;
   const int hq1 = split ? (part & 1) : 1;
@@ -428,8 +321,8 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
       if (!row_ok && !ep.tma_c) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        lo[i] *= alpha;
-        hi[i] *= alpha;
+        lo[i] *= ep.alpha;
+        hi[i] *= ep.alpha;
       }
       if (ep.bias != nullptr) {  // the same address on every lane: one broadcast load
         float b[8];
@@ -496,11 +389,11 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, int part,
                                               int nparts, const CUtensorMap* tmC, const CUtensorMap* tmR,
-                                              EpiStore& es, int lane, float alpha, float amu) {
+                                              EpiStore& es, int lane) {
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
-    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts, tmC, es, lane, alpha);
+    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts, tmC, es, lane);
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
     for (int c = 32 * part; c < BN; c += 32 * nparts) {
@@ -511,7 +404,7 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       if (n >= ep.N) break;
       if (!row_ok && !ep.tma_c) continue;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * alpha) * (u[i] * alpha);
+      for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * ep.alpha) * (u[i] * ep.alpha);
       const int nc = n >> 1;
       if (ep.residual != nullptr && row_ok) {
         const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + nc);
@@ -555,22 +448,8 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
         prefetch32(ep, m, n + step, row_ok, nxt);
         if (ep.tma_r) res_load(tmR, es, es.sb ^ 1, n + step, rrow, 0, lane);
       }
-      if (ep.norm == VLA_NORM_LN) {
-        // rstd * (acc - mu * colsum(B)): the raw row's mean taken out after the product
-        const float4* cs4 = reinterpret_cast<const float4*>(ep.norm_colsum + n);
-        const int ncs = 2 * chunk_vecs(ep, n);  // float4s of colsum inside [0, N)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 cs = __ldg(cs4 + (i < ncs ? i : 0));
-          v[4 * i] = fmaf(-amu, cs.x, v[4 * i] * alpha);
-          v[4 * i + 1] = fmaf(-amu, cs.y, v[4 * i + 1] * alpha);
-          v[4 * i + 2] = fmaf(-amu, cs.z, v[4 * i + 2] * alpha);
-          v[4 * i + 3] = fmaf(-amu, cs.w, v[4 * i + 3] * alpha);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= alpha;
-      }
+      for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
       finish32(ep, m, n, orow, v, row_ok, cur, tmC, es, lane);
       if (more) cur = nxt;
     }
@@ -589,15 +468,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * Cf::A_BYTES;
   uint8_t* sC = sB + STAGES * Cf::B_BYTES;  // output staging (1024-byte aligned)
-  float2* nstat = reinterpret_cast<float2*>(sC + kEpiStoreBytes);  // [BM] row (mean, rstd)
-  uint64_t* full = reinterpret_cast<uint64_t*>(sC + kEpiStoreBytes + kNormBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + kEpiStoreBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;  // [kEpiWarps][2]: residual chunk landed
-  uint64_t* nfull = rbar + 2 * kEpiWarps;  // row statistics of the tile ready
-  uint64_t* nempty = nfull + 1;            // epilogue has read them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(nempty + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -610,15 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ep.norm ? 1 + kStatWarps : 1);  // MMA commit (+ statistics warps)
+      mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 32 * kEpiWarps);
     }
     for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
-    mbar_init(nfull, kStatWarps);
-    mbar_init(nempty, kEpiWarps);
     *abort_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
@@ -703,14 +577,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
       }
     }
-  } else if (warp >= 2 + kEpiWarps) {
-    // ---- row statistics of the A tiles (folded RMSNorm / LayerNorm) ----
-    if (ep.norm && !stat_warps(ep, sA, Cf::A_BYTES, STAGES, full, false, empty, nstat, nfull, nempty, abort_flag,
-                               blockIdx.x, gridDim.x, num_tiles, num_kb, (warp - 2 - kEpiWarps) * 64 + lane, lane) &&
-        lane == 0) {
-      if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_EPILOGUE_TIMEOUT);
-      *abort_flag = 1;
-    }
   } else {
     const int q = warp & 3;               // TMEM lane quarter this warp may access
     const int part = (warp - 2) >> 2;     // which column share of that quarter
@@ -733,16 +599,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = mb * BM + q * 32 + lane;
       es.row0 = mb * BM + q * 32;
-      float alpha, amu;
-      if (!norm_row_scale(ep, nstat, nfull, nempty, abort_flag, tc, q * 32 + lane, lane, alpha, amu)) {
-        if (lane == 0) {
-          if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_EPILOGUE_TIMEOUT);
-          *abort_flag = 1;
-        }
-        break;
-      }
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane, alpha, amu);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
       tc_fence_before();
       mbar_arrive(&tempty[as]);
       ++tc;

@@ -24,14 +24,12 @@ struct Cfg2 {
   static constexpr int A_BYTES = BM * BK * 2;        // 128 rows of A per CTA
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // half of the B tile per CTA
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes - kNormBytes;
+  static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kNormBytes + kBarrierBytes + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "UMMA N");
   static_assert(B_BYTES % 1024 == 0, "B half-tile alignment (BN/2 multiple of 8)");
-  static_assert((3 * STAGES + 4 + 2 * kEpiWarps + 2) * 8 + 8 <= kBarrierBytes, "barrier area");
-  static_assert(BN != 256 || STAGES == 6, "pipeline depth of the 256-wide pair tile");
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -107,16 +105,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * Cf::A_BYTES;
   uint8_t* sC = sB + STAGES * Cf::B_BYTES;  // output staging (1024-byte aligned)
-  float2* nstat = reinterpret_cast<float2*>(sC + kEpiStoreBytes);  // [BM] row (mean, rstd)
-  uint64_t* full = reinterpret_cast<uint64_t*>(sC + kEpiStoreBytes + kNormBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sC + kEpiStoreBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;  // [kEpiWarps][2]: residual chunk landed (this CTA's)
-  uint64_t* afull = rbar + 2 * kEpiWarps;  // [STAGES] (rank 1): the leader saw stage s land
-  uint64_t* nfull = afull + STAGES;        // row statistics of the tile ready
-  uint64_t* nempty = nfull + 1;            // epilogue has read them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(nempty + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -132,11 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 2);   // one expect_tx arrival per CTA (leader's copy is used)
-      mbar_init(&empty[s], ep.norm ? 1 + kStatWarps : 1);  // multicast MMA commit (+ statistics warps)
-      mbar_init(&afull[s], 1);
+      mbar_init(&empty[s], 1);  // multicast MMA commit
     }
-    mbar_init(nfull, kStatWarps);
-    mbar_init(nempty, kEpiWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);                    // multicast MMA commit
       mbar_init(&tempty[i], 2 * kEpiWarps);  // one arrival per epilogue warp of both CTAs (leader's copy)
@@ -233,18 +224,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
       }
     }
-  } else if (warp >= 2 + kEpiWarps) {
-    // ---- row statistics of this CTA's A rows (folded RMSNorm / LayerNorm) ----
-    // the leader's first statistics warp passes each stage's arrival on to the
-    // peer, whose A rows completed on the leader's barrier
-    const uint32_t relay = (rank == 0 && warp == 2 + kEpiWarps) ? map_to_rank(smem_u32(afull), 1) : 0u;
-    if (ep.norm && !stat_warps(ep, sA, Cf::A_BYTES, STAGES, rank == 0 ? full : afull, rank != 0, empty, nstat, nfull,
-                               nempty, abort_flag, cluster, n_clusters, num_tiles, num_kb,
-                               (warp - 2 - kEpiWarps) * 64 + lane, lane, relay) &&
-        lane == 0) {
-      if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_EPILOGUE_TIMEOUT);
-      *abort_flag = 1;
-    }
   } else {
     const int q = warp & 3;
     const int part = (warp - 2) >> 2;
@@ -269,16 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = mb * 2 * BM + (int)rank * BM + q * 32 + lane;
       es.row0 = mb * 2 * BM + (int)rank * BM + q * 32;
-      float alpha, amu;
-      if (!norm_row_scale(ep, nstat, nfull, nempty, abort_flag, tc, q * 32 + lane, lane, alpha, amu)) {
-        if (lane == 0) {
-          if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_EPILOGUE_TIMEOUT);
-          *abort_flag = 1;
-        }
-        break;
-      }
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane, alpha, amu);
+      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster_relaxed(as ? leader_tempty1 : leader_tempty0);

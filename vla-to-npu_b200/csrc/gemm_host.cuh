@@ -164,11 +164,7 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
     ep.euler_x = e->euler_x;
     ep.ldx = e->ldx;
     ep.euler_dt = e->euler_dt;
-    ep.norm = e->norm;
-    ep.norm_eps = e->norm_eps;
-    ep.norm_colsum = e->norm_colsum;
   }
-  ep.K = (int)K;
   ep.act = act;
   VLA_CHECK_ARG(act >= VLA_ACT_NONE && act <= VLA_ACT_EULER, "gemm: unknown act %d", act);
   const int64_t out_cols = act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -186,17 +182,6 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
     VLA_CHECK_ARG(ep.rope_cs && ep.rope_seq > 0, "gemm: RoPE needs a cos/sin table and rope_seq > 0");
     VLA_CHECK_ARG(ep.rope_ncols % 64 == 0 && ep.rope_ncols <= N, "gemm: rope_ncols must be a multiple of 64 <= N");
     VLA_CHECK_ARG(N % 64 == 0, "gemm: RoPE needs N %% 64 == 0");
-  }
-  VLA_CHECK_ARG(ep.norm >= VLA_NORM_NONE && ep.norm <= VLA_NORM_LN, "gemm: unknown norm %d", ep.norm);
-  if (ep.norm) {
-    VLA_CHECK_ARG(act != VLA_ACT_EULER, "gemm: a folded norm does not combine with the Euler epilogue");
-    VLA_CHECK_ARG(ep.norm_eps >= 0.f, "gemm: norm_eps must be >= 0");
-  }
-  if (ep.norm == VLA_NORM_LN) {
-    VLA_CHECK_ARG(ep.norm_colsum != nullptr, "gemm: LayerNorm folding needs norm_colsum[N]");
-    VLA_CHECK_ALIGN(aligned16(ep.norm_colsum), "gemm: norm_colsum must be 16-byte aligned");
-    VLA_CHECK_ARG(act == VLA_ACT_NONE || act == VLA_ACT_GELU_TANH,
-                  "gemm: LayerNorm folding supports the plain / bias / GELU / residual epilogues");
   }
   if (act == VLA_ACT_EULER) {
     VLA_CHECK_ARG(ep.euler_x != nullptr && ep.ldx >= N, "gemm: Euler needs an fp32 state with ldx >= N");

@@ -25,9 +25,6 @@ ACT_GELU_TANH = 1
 ACT_SWIGLU = 2
 ACT_ROPE = 3
 ACT_EULER = 4
-NORM_NONE = 0
-NORM_RMS = 1
-NORM_LN = 2
 
 
 class VlaError(RuntimeError):
@@ -56,9 +53,7 @@ class Epilogue(ctypes.Structure):
         ("euler_x", ctypes.c_void_p),
         ("ldx", ctypes.c_int64),
         ("euler_dt", ctypes.c_float),
-        ("norm", ctypes.c_int32),
-        ("norm_eps", ctypes.c_float),
-        ("norm_colsum", ctypes.c_void_p),
+        ("reserved", ctypes.c_int32 * 4),
     ]
 
 

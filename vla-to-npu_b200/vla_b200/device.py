@@ -32,8 +32,7 @@ def _rowmajor(t: torch.Tensor, name: str) -> int:
 
 
 def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, alpha=1.0, rope_cs=None, rope_seq=0,
-                  rope_ncols=0, out_grp=0, out_grp_stride=0, euler_x=None, euler_dt=0.0, norm=0, norm_eps=0.0,
-                  norm_colsum=None) -> Epilogue:
+                  rope_ncols=0, out_grp=0, out_grp_stride=0, euler_x=None, euler_dt=0.0) -> Epilogue:
     e = Epilogue()
     e.bias = None if bias is None else bias.data_ptr()
     e.residual = None if residual is None else residual.data_ptr()
@@ -49,9 +48,6 @@ def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, al
     e.euler_x = None if euler_x is None else euler_x.data_ptr()
     e.ldx = 0 if euler_x is None else _rowmajor(euler_x, "euler_x")
     e.euler_dt = euler_dt
-    e.norm = norm
-    e.norm_eps = norm_eps
-    e.norm_colsum = None if norm_colsum is None else norm_colsum.data_ptr()
     return e
 
 
