@@ -30,13 +30,11 @@ static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const vo
                   "norm: 16-byte alignment");
   if (M == 0) return VLA_OK;
   const int grid = (int)((M + norm::kWarps - 1) / norm::kWarps);
+  const bf16* bb = mode == 0 ? nullptr : (const bf16*)b;
+  auto kern = mode == 0 ? norm::rownorm_kernel<0> : norm::rownorm_kernel<1>;
   prof_begin(st);
-  if (mode == 0)
-    launch_k(norm::rownorm_kernel<0>, dim3(grid), dim3(norm::kWarps * 32), 0, st, (const bf16*)x, ldx, (const bf16*)g, nullptr,
-                                                                 (bf16*)y, ldy, (int)M, (int)N, eps);
-  else
-    launch_k(norm::rownorm_kernel<1>, dim3(grid), dim3(norm::kWarps * 32), 0, st, (const bf16*)x, ldx, (const bf16*)g, (const bf16*)b,
-                                                                 (bf16*)y, ldy, (int)M, (int)N, eps);
+  launch_k(kern, dim3(grid), dim3(norm::kWarps * 32), 0, st, (const bf16*)x, ldx, (const bf16*)g, bb, (bf16*)y, ldy,
+           (int)M, (int)N, eps);
   prof_end(st, VLA_KIND_NORM, 0.0, 4.0 * (double)M * N);
   return launch_status("rownorm");
 }
