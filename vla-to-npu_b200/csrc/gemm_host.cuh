@@ -98,6 +98,32 @@ static int choose_ctas(int64_t M, int bn) {
   return (M >= 32 * BM && bn >= 64) ? 2 : 1;
 }
 
+// Tile width of a CTA-pair launch.  A k-block of the pair's main loop costs
+// about the same time for every width up to 256 (the copies' loaded latency,
+// not the 256 x BN x 64 MMA, sets its pace: measured ~555 SM cycles per k-block
+// at BN = 192 and 256), so a tile's time hardly depends on BN and the launch
+// time follows the number of waves of 256 x BN tiles over the pairs.  Take the
+// fewest waves; among equal counts the least padding past N, then the widest
+// tile (fewer tiles, fewer epilogue passes).
+static int choose_bn_pair(int64_t M, int64_t N, int act, int num_sms) {
+  const int cands[5] = {256, 224, 192, 160, 128};
+  const int64_t pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
+  int best = 0;
+  int64_t best_waves = 0, best_padded = 0;
+  for (int bn : cands) {
+    if (act == VLA_ACT_ROPE && bn % 64 != 0) continue;
+    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    const int64_t padded = ((N + bn - 1) / bn) * bn;
+    if (best == 0 || waves < best_waves || (waves == best_waves && padded < best_padded)) {
+      best = bn;
+      best_waves = waves;
+      best_padded = padded;
+    }
+  }
+  return best;
+}
+
 template <int BN>
 static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const CUtensorMap& tr,
                      const DevEpi& ep,
@@ -219,7 +245,7 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                            CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   }
-  const int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
+  int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
   // VLA_GEMM_CTAS=1|2 overrides the automatic one-CTA / pair choice (A/B measurement)
   static const int env_ctas = [] {
     const char* v = getenv("VLA_GEMM_CTAS");
@@ -228,6 +254,7 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   const int ctas = force_ctas                          ? force_ctas
                    : (env_ctas == 1 || env_ctas == 2) ? env_ctas
                                                       : choose_ctas(M, bn);
+  if (ctas == 2 && !force_bn) bn = choose_bn_pair(M, N, act, device_info().num_sms);
   if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
   if (ctas == 2) {
     switch (bn) {
