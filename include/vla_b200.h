@@ -222,14 +222,16 @@ typedef struct vla_attention_args {
   int32_t causal;
   const int32_t* kv_len; /* device int32 [batch] or NULL */
   float scale;
-  int32_t impl;          /* VLA_ATTN_AUTO, VLA_ATTN_MMA_SYNC or VLA_ATTN_TCGEN05 */
+  int32_t impl;          /* VLA_ATTN_AUTO, _MMA_SYNC, _TCGEN05 or _TCGEN05_SHORT */
 } vla_attention_args;
 /* Attention kernels: AUTO picks the tcgen05 kernel (persistent, 128-row query
- * tiles, TMEM accumulators) for non-causal attention with Lk >= 256 and the
- * mma.sync kernel (64-row tiles) otherwise; TCGEN05 supports non-causal
- * attention only and needs q_batch / k_batch / v_batch to be whole multiples of
- * the row strides. */
-enum { VLA_ATTN_AUTO = 0, VLA_ATTN_MMA_SYNC = 1, VLA_ATTN_TCGEN05 = 2 };
+ * tiles, TMEM accumulators) for non-causal attention with Lk >= 256, the
+ * short-sequence tcgen05 kernel (all keys of a sequence in one tile, the query
+ * heads of a kv head stacked into 128-row tiles) for Lk <= 128, causal or not,
+ * and the mma.sync kernel (64-row tiles) otherwise.  TCGEN05 supports
+ * non-causal attention only and needs q_batch / k_batch / v_batch to be whole
+ * multiples of the row strides; TCGEN05_SHORT needs Lk <= 128. */
+enum { VLA_ATTN_AUTO = 0, VLA_ATTN_MMA_SYNC = 1, VLA_ATTN_TCGEN05 = 2, VLA_ATTN_TCGEN05_SHORT = 3 };
 int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream);
 
 /* Pixel shuffle: in [B, grid*grid, C] -> out [B, (grid/s)^2, s*s*C] with

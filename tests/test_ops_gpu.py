@@ -256,3 +256,34 @@ def test_attention_tcgen05_strided_qkv(cuda):
         ref = R.attention(x[b:b + 1, :, 0], x[b:b + 1, :, 1], x[b:b + 1, :, 2], causal=False,
                           dt=torch.float32).reshape(L, -1)
         torch.testing.assert_close(o[b * L:(b + 1) * L].float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("Lq,Lk,Hq,Hkv,causal,B,kv_len", [
+    (113, 113, 15, 5, True, 3, None),        # C4 prefix: 3 x 113 stacked rows, causal
+    (128, 128, 15, 5, True, 1, None),        # C0 text: 384 stacked rows, 128 keys
+    (50, 50, 15, 5, True, 2, None),          # C3 expert self: 64-key variant
+    (50, 113, 15, 5, False, 3, [113, 60, 1]),  # C3 expert cross with key padding
+    (50, 128, 15, 5, False, 2, [0, 128]),      # a sequence with no keys writes zeros
+    (7, 33, 4, 2, False, 1, None),            # ragged: 14 stacked rows, 33 keys
+    (300, 97, 2, 2, True, 2, None),           # one head per kv head, 3 row tiles
+])
+def test_attention_tcgen05_short(cuda, Lq, Lk, Hq, Hkv, causal, B, kv_len):
+    """The short-sequence tcgen05 kernel (all keys in one tile, query heads of a
+    kv head stacked into 128-row tiles) forced on, against the fp32 oracle."""
+    from vla_b200 import _lib, device as dev
+    q = _rand((B, Lq, Hq, 64), 31)
+    k = _rand((B, Lk, Hkv, 64), 32)
+    v = _rand((B, Lk, Hkv, 64), 33)
+    o = torch.full((B * Lq, Hq * 64), float("nan"), dtype=BF, device="cuda")
+    kl = None if kv_len is None else torch.tensor(kv_len, dtype=torch.int32, device="cuda")
+    dev.attention(q.reshape(B * Lq, -1).cuda(), k.reshape(B * Lk, -1).cuda(), v.reshape(B * Lk, -1).cuda(), o,
+                  batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=Lq * Hq * 64, k_batch=Lk * Hkv * 64,
+                  v_batch=Lk * Hkv * 64, o_batch=Lq * Hq * 64, causal=causal, kv_len=kl,
+                  impl=_lib.ATTN_TCGEN05_SHORT)
+    dev.sync_check()
+    ref = R.attention(q, k, v, causal=causal, kv_len=kv_len, dt=torch.float32).reshape(B * Lq, -1)
+    if kv_len is not None and 0 in kv_len:
+        ref = ref.view(B, Lq, -1)
+        ref[[i for i, n in enumerate(kv_len) if n == 0]] = 0.0
+        ref = ref.reshape(B * Lq, -1)
+    torch.testing.assert_close(o.float().cpu(), ref, atol=2e-2, rtol=2e-2)

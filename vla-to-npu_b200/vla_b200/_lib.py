@@ -74,6 +74,7 @@ class AttentionArgs(ctypes.Structure):
 ATTN_AUTO = 0
 ATTN_MMA_SYNC = 1
 ATTN_TCGEN05 = 2
+ATTN_TCGEN05_SHORT = 3
 
 
 class LlamaLayer(ctypes.Structure):
