@@ -76,6 +76,7 @@ KERNEL_CASES = {
     "gemm_exp_qkv": "action-expert self-attention QKV + RoPE on Q and K, M=12800 N=1600 K=720",
     "gemm_exp_gu": "action-expert gate/up + SwiGLU, M=12800 N=4096 K=720",
     "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
+    "attn_text": "text-prefix causal GQA attention (short-sequence tcgen05 kernel), 256 x 15 q / 5 kv heads x 113 x 113",
     "layer_norm": "SigLIP LayerNorm, 16384 x 768",
 }
 
@@ -120,6 +121,17 @@ def run_kernel_case(args):
                                    batch=B, Lq=L, Lk=L, Hq=H, Hkv=H, q_batch=L * 3 * H * 64, k_batch=L * 3 * H * 64,
                                    v_batch=L * 3 * H * 64, o_batch=L * H * 64)
         flops, nbytes = 4.0 * B * H * L * L * 64, 2.0 * B * L * H * 64 * 4
+    elif name == "attn_text":
+        # the step's own shape (256 observations, 148 MB): 16 would leave most SMs idle
+        B, L, Hq, Hkv = 256, 113, 15, 5
+        cols = (Hq + 2 * Hkv) * 64
+        qkv = W.randn((B * L, cols), 0, "kc.qkv").cuda()
+        o = torch.empty(B * L, Hq * 64, dtype=bf, device="cuda")
+        fn = lambda: dev.attention(qkv[:, :Hq * 64], qkv[:, Hq * 64:(Hq + Hkv) * 64],  # noqa: E731
+                                   qkv[:, (Hq + Hkv) * 64:], o, batch=B, Lq=L, Lk=L, Hq=Hq, Hkv=Hkv,
+                                   q_batch=L * cols, k_batch=L * cols, v_batch=L * cols, o_batch=L * Hq * 64,
+                                   causal=True)
+        flops, nbytes = 4.0 * B * Hq * L * L * 64, 2.0 * B * L * (2 * Hq + 2 * Hkv) * 64
     else:
         x = W.randn((16384, 768), 0, "kc.x").cuda()
         g, bb = torch.ones(768, dtype=bf, device="cuda"), torch.zeros(768, dtype=bf, device="cuda")
