@@ -117,6 +117,23 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (j << 23));
 }
 
+// Packed fp32 pairs (one instruction for two lanes' worth of FMA-pipe work):
+// (x0, x1) = (a0, a1) * b + c, and (s0, s1) += (e0, e1).
+__device__ __forceinline__ void fma2(float a0, float a1, float b, float c, float& x0, float& x1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float e0, float e1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(e0), "f"(e1));
+}
+
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -498,8 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[BKV / 2];
 #pragma unroll
         for (int c = 0; c < BKV; c += 2) {
-          const float x0 = fmaf(sr[c], p.scale_log2, -mbase);
-          const float x1 = fmaf(sr[c + 1], p.scale_log2, -mbase);
+          float x0, x1;
+          fma2(sr[c], sr[c + 1], p.scale_log2, -mbase, x0, x1);
           const bool poly = kPolyPeriod > 0 && ((c >> 1) % (kPolyPeriod > 0 ? kPolyPeriod : 1)) == 0;
           const float e0 = poly ? ex2_poly(x0) : ex2_fast(x0);
           const float e1 = poly ? ex2_poly(x1) : ex2_fast(x1);
@@ -507,8 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             rs8[c & 7] = e0;
             rs8[(c + 1) & 7] = e1;
           } else {
-            rs8[c & 7] += e0;
-            rs8[(c + 1) & 7] += e1;
+            add2(rs8[c & 7], rs8[(c + 1) & 7], e0, e1);
           }
           pk[c >> 1] = pack_bf16x2(e0, e1);
         }
