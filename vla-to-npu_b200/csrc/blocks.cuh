@@ -30,7 +30,11 @@ static int rownorm(int mode, const void* x, int64_t ldx, const void* g, const vo
   VLA_CHECK_ALIGN(ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(g) && (!b || aligned16(b)),
                   "norm: 16-byte alignment");
   if (M == 0) return VLA_OK;
-  const int grid = (int)((M + norm::kWarps - 1) / norm::kWarps);
+  // a resident grid (8 CTAs of 8 warps per SM) walking the rows: 3-5 % faster
+  // than one short-lived CTA per 8 rows (SigLIP LayerNorm 151 -> 144 us)
+  const int64_t blocks = (M + norm::kWarps - 1) / norm::kWarps;
+  const int64_t cap = 8ll * device_info().num_sms;
+  const int grid = (int)(blocks < cap ? blocks : cap);
   const bf16* bb = mode == 0 ? nullptr : (const bf16*)b;
   auto kern = mode == 0 ? norm::rownorm_kernel<0> : norm::rownorm_kernel<1>;
   prof_begin(st);

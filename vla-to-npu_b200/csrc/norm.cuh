@@ -154,7 +154,8 @@ __device__ __forceinline__ void norm_row_wide(const bf16* __restrict__ x, long l
   }
 }
 
-// MODE 0 = RMSNorm, 1 = LayerNorm; one warp per row.
+// MODE 0 = RMSNorm, 1 = LayerNorm; one warp per row, the grid striding over
+// the rows.
 template <int MODE>
 __global__ void __launch_bounds__(kWarps * 32) rownorm_kernel(const bf16* __restrict__ x, long long ldx,
                                                               const bf16* __restrict__ g, const bf16* __restrict__ b,
@@ -162,12 +163,12 @@ __global__ void __launch_bounds__(kWarps * 32) rownorm_kernel(const bf16* __rest
                                                               float eps) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * kWarps + warp;
-  if (row >= M) return;
-  if ((N >> 3) <= 32 * kMaxVec)
-    norm_rows_reg<MODE, 1>(x, ldx, g, b, y, ldy, row, M, N, eps, lane);
-  else
-    norm_row_wide<MODE>(x, ldx, g, b, y, ldy, row, N, eps, lane);
+  for (long long row = (long long)blockIdx.x * kWarps + warp; row < M; row += (long long)gridDim.x * kWarps) {
+    if ((N >> 3) <= 32 * kMaxVec)
+      norm_rows_reg<MODE, 1>(x, ldx, g, b, y, ldy, row, M, N, eps, lane);
+    else
+      norm_row_wide<MODE>(x, ldx, g, b, y, ldy, row, N, eps, lane);
+  }
 }
 
 }  // namespace norm
