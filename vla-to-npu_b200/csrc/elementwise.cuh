@@ -108,16 +108,18 @@ __global__ void act_kernel(const bf16* __restrict__ x, long long ldx, const bf16
 // the reshape/transpose chain of con_ref (vla/vla.py:434-436) and the copy
 // regions of fused_op (vla/connector_bf16.py:97-111).  Vectorised over c.
 // ---------------------------------------------------------------------------
+// I: index type of the vector counter (32-bit when the total fits: the
+// divisions below dominate the kernel's cost in 64-bit arithmetic)
+template <typename I>
 __global__ void pixel_shuffle_kernel(const bf16* __restrict__ in, bf16* __restrict__ out, int B, int grid, int s,
                                      int C) {
   pdl_prologue();
   const int cv = C >> 3;
-  const long long total = (long long)B * grid * grid * cv;
+  const I total = (I)B * grid * grid * cv;
   const int g2 = grid / s;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
     const int c = (int)(i % cv) * 8;
-    long long tok = i / cv;
+    I tok = i / cv;
     const int w = (int)(tok % grid);
     tok /= grid;
     const int h = (int)(tok % grid);
@@ -136,25 +138,25 @@ __global__ void pixel_shuffle_kernel(const bf16* __restrict__ in, bf16* __restri
 // cc/bf16_old/conv_bf16.cc:12-55 computes the same dot products per patch).
 // Vectorised over 8 consecutive kx.
 // ---------------------------------------------------------------------------
+template <typename I>
 __global__ void im2col_kernel(const bf16* __restrict__ img, bf16* __restrict__ out, int B, int Cin, int H, int W,
                               int p) {
   pdl_prologue();
   const int gh = H / p, gw = W / p;
   const int kdim = Cin * p * p;
   const int vec_per_row = kdim >> 3;
-  const long long total = (long long)B * gh * gw * vec_per_row;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
+  const I total = (I)B * gh * gw * vec_per_row;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
     const int col = (int)(i % vec_per_row) * 8;
-    const long long tok = i / vec_per_row;
+    const I tok = i / vec_per_row;
     const int px = (int)(tok % gw);
     const int py = (int)((tok / gw) % gh);
-    const long long b = tok / ((long long)gw * gh);
+    const long long b = tok / ((I)gw * gh);
     const int cin = col / (p * p);
     const int ky = (col / p) % p;
     const int kx = col % p;
     const bf16* src = img + ((b * Cin + cin) * H + (py * p + ky)) * (long long)W + px * p + kx;
-    *reinterpret_cast<uint4*>(out + tok * kdim + col) = *reinterpret_cast<const uint4*>(src);
+    *reinterpret_cast<uint4*>(out + (long long)tok * kdim + col) = *reinterpret_cast<const uint4*>(src);
   }
 }
 

@@ -239,8 +239,10 @@ int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, i
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * grid * grid * (C / 8);
   prof_begin(as_stream(stream));
-  launch_k(ew::pixel_shuffle_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)in, (bf16*)out,
-                                                                                       B, grid, scale, C);
+  // 32-bit vector counter while it cannot overflow (with the grid stride added)
+  auto ps_kern = work < (1ll << 30) ? ew::pixel_shuffle_kernel<int> : ew::pixel_shuffle_kernel<long long>;
+  launch_k(ps_kern, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)in, (bf16*)out, B,
+           grid, scale, C);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * grid * grid * C);
   return launch_status("pixel_shuffle");
 }
@@ -253,8 +255,9 @@ int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, in
   if (B == 0) return VLA_OK;
   const long long work = (long long)B * (H / p) * (W / p) * (Cin * p * p / 8);
   prof_begin(as_stream(stream));
-  launch_k(ew::im2col_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)img, (bf16*)out, B, Cin,
-                                                                                H, W, p);
+  auto ic_kern = work < (1ll << 30) ? ew::im2col_kernel<int> : ew::im2col_kernel<long long>;
+  launch_k(ic_kern, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), (const bf16*)img, (bf16*)out, B,
+           Cin, H, W, p);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 4.0 * (double)B * Cin * H * W);
   return launch_status("im2col");
 }
