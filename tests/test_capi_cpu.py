@@ -54,6 +54,20 @@ def test_host_validation_without_gpu():
     a = _lib.AttentionArgs()
     a.head_dim = 128
     assert lib.vla_attention_bf16(ctypes.byref(a), None) == _lib.VLA_E_INVALID
+    # a well-formed call except for the kernel choice: unknown impl, and the
+    # short-sequence tcgen05 kernel forced on with more than 128 keys
+    a = _lib.AttentionArgs()
+    a.q = a.k = a.v = a.o = 256
+    a.q_row, a.k_row, a.v_row, a.o_row = 960, 320, 320, 960
+    a.q_batch, a.k_batch, a.v_batch, a.o_batch = 960 * 50, 320 * 200, 320 * 200, 960 * 50
+    a.batch, a.Lq, a.Lk, a.Hq, a.Hkv, a.head_dim = 2, 50, 200, 15, 5, 64
+    a.scale = 0.125
+    a.impl = 4
+    assert lib.vla_attention_bf16(ctypes.byref(a), None) == _lib.VLA_E_INVALID
+    assert "impl" in _lib.last_error()
+    a.impl = _lib.ATTN_TCGEN05_SHORT
+    assert lib.vla_attention_bf16(ctypes.byref(a), None) == _lib.VLA_E_INVALID
+    assert "128" in _lib.last_error()
 
 
 def test_rope_table_host_helper_matches_model_table():
