@@ -78,6 +78,10 @@ KERNEL_CASES = {
     "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
     "attn_text": "text-prefix causal GQA attention (short-sequence tcgen05 kernel), 256 x 15 q / 5 kv heads x 113 x 113",
     "layer_norm": "SigLIP LayerNorm, 16384 x 768",
+    "rms_norm": "text-width RMSNorm, 131072 x 960 (250 MB in, larger than L2)",
+    "attn_exp_self": "action-expert causal self-attention, 512 x 15 q / 5 kv heads x 50 x 50 (AUTO kernel choice)",
+    "attn_exp_cross": "action-expert cross-attention to the prefix, 512 x 15 q / 5 kv heads x 50 x 113 (AUTO)",
+    "gemm_fc1_full": "SigLIP fc1 GEMM + bias + GELU at the bench step's shape, M=262144 N=3072 K=768 (2 GB)",
 }
 
 
@@ -91,7 +95,7 @@ def run_kernel_case(args):
         raise SystemExit(f"unknown kernel case {name!r}; choose from {list(KERNEL_CASES)}")
     bf = torch.bfloat16
     if name.startswith("gemm"):
-        M, N, K = {"gemm_fc1": (16384, 3072, 768), "gemm_qkv": (16384, 2304, 768),
+        M, N, K = {"gemm_fc1": (16384, 3072, 768), "gemm_fc1_full": (262144, 3072, 768), "gemm_qkv": (16384, 2304, 768),
                    "gemm_fc2": (16384, 768, 3072), "gemm_plain": (16384, 3072, 768),
                    "gemm_plain_k3072": (16384, 3072, 3072), "gemm_exp_down": (12800, 720, 2048),
                    "gemm_exp_o": (12800, 720, 960), "gemm_exp_qkv": (12800, 1600, 720),
@@ -103,7 +107,7 @@ def run_kernel_case(args):
         res = W.randn((M, N), 0, "kc.r").cuda() if name in ("gemm_fc2", "gemm_exp_down", "gemm_exp_o") else None
         plain = name.startswith("gemm_plain") or name.startswith("gemm_exp")
         epi = dev.make_epilogue(bias=None if plain else b, residual=res,
-                                act=_lib.ACT_GELU_TANH if name == "gemm_fc1" else 0)
+                                act=_lib.ACT_GELU_TANH if name.startswith("gemm_fc1") else 0)
         if name == "gemm_exp_qkv":
             from vla_b200.model import rope_table
             cs = rope_table(50, 64, 10_000.0).cuda()
@@ -132,6 +136,29 @@ def run_kernel_case(args):
                                    q_batch=L * cols, k_batch=L * cols, v_batch=L * cols, o_batch=L * Hq * 64,
                                    causal=True)
         flops, nbytes = 4.0 * B * Hq * L * L * 64, 2.0 * B * L * (2 * Hq + 2 * Hkv) * 64
+    elif name in ("attn_exp_self", "attn_exp_cross"):
+        B, Lq, Hq, Hkv = 512, 50, 15, 5
+        Lk = Lq if name == "attn_exp_self" else 113
+        if name == "attn_exp_self":
+            cols = (Hq + 2 * Hkv) * 64
+            qkv = W.randn((B * Lq, cols), 0, "kc.qkv").cuda()
+            q, k, v = qkv[:, :Hq * 64], qkv[:, Hq * 64:(Hq + Hkv) * 64], qkv[:, (Hq + Hkv) * 64:]
+            qb = kb = Lq * cols
+        else:
+            q = W.randn((B * Lq, Hq * 64), 0, "kc.q").cuda()
+            kv = W.randn((B * Lk, 2 * Hkv * 64), 0, "kc.kv").cuda()
+            k, v = kv[:, :Hkv * 64], kv[:, Hkv * 64:]
+            qb, kb = Lq * Hq * 64, Lk * 2 * Hkv * 64
+        o = torch.empty(B * Lq, Hq * 64, dtype=bf, device="cuda")
+        fn = lambda: dev.attention(q, k, v, o, batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=qb,  # noqa: E731
+                                   k_batch=kb, v_batch=kb, o_batch=Lq * Hq * 64, causal=name == "attn_exp_self")
+        flops, nbytes = 4.0 * B * Hq * Lq * Lk * 64, 2.0 * B * (2 * Lq * Hq + 2 * Lk * Hkv) * 64
+    elif name == "rms_norm":
+        x = W.randn((131072, 960), 0, "kc.x").cuda()
+        g = torch.ones(960, dtype=bf, device="cuda")
+        y = torch.empty_like(x)
+        fn = lambda: dev.rms_norm(x, g, 1e-5, out=y)  # noqa: E731
+        flops, nbytes = 0.0, 4.0 * 131072 * 960
     else:
         x = W.randn((16384, 768), 0, "kc.x").cuda()
         g, bb = torch.ones(768, dtype=bf, device="cuda"), torch.zeros(768, dtype=bf, device="cuda")

@@ -89,6 +89,13 @@ int vla_version(void);
 int vla_sync_check(void);
 /* Device error word without clearing (0 = none). */
 int vla_peek_device_error(unsigned int* code);
+/* Exercises the device error channel without a fault: launches one block whose
+ * thread waits on an mbarrier that nothing ever completes, with a time limit of
+ * limit_us microseconds (1 .. 1000000); the wait runs out, the kernel records
+ * the test code 0x1FF in the device error word and returns.  A following
+ * vla_sync_check() then reports VLA_E_DEVICE_TIMEOUT.  No counterpart in the
+ * reference (its NPU calls have no error channel). */
+int vla_test_expired_wait(int32_t limit_us, vla_stream_t stream);
 /* sizeof of the ABI structs, in the order vla_epilogue, vla_attention_args,
  * vla_llama_layer, vla_vision_layer, vla_profile_record, written to out[0..n);
  * returns the count. */
@@ -317,7 +324,9 @@ int vla_llama_cross_layer_bf16(const vla_llama_layer* w, void* x, int32_t batch,
  *   The call itself allocates nothing.
  * - The first call on each device looks up the array's device address
  *   (cudaGetSymbolAddress) with that device current; make that first call
- *   before any stream capture on the device.
+ *   before any stream capture on the device.  The address is cached for the
+ *   life of the process: after cudaDeviceReset on a device this entry point
+ *   must not be called on that device again.
  * - All calls share the one array and it keeps the previous call's
  *   contents (nothing in it needs to start at zero).  Two calls whose
  *   kernels overlap on the GPU (different streams, or different host

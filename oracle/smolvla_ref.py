@@ -11,6 +11,9 @@ serve as its own correctness oracle:
 * apply_rope (half-split)       vla/text_encoder_bf16.py:92-104
 * ActionExpertSelfBlock         vla/action_expert_bf16.py:69-131
 * ActionExpertCrossBlock        vla/action_expert_bf16.py:137-207
+* CrossAttentionBlock           vla/llama_block_rope_bf16.py:133-180
+* llama_block_rope_cross        vla/llama_block_rope_bf16.py:617-709 (the
+  Allo cross path: RoPE on Q and on the given key, causal mask)
 * MiniVit (block skeleton)      vla/vision_block_bf16.py:57-79, with the real
   SigLIP layer of vla/vision_block.py:4-30 (biases, LayerNorm eps 1e-6,
   GELU-tanh)
@@ -260,6 +263,56 @@ def expert_cross_block(x, kc, vc, p, cfg, kv_len=None, dt=F32):
     return swiglu_mlp(h, p, dt) + residual
 
 
+def cross_attention_block(x, context, p, cfg, dt=F32):
+    """CrossAttentionBlock.forward (vla/llama_block_rope_bf16.py:133-180): the
+    context is normalised by the same ln_1 as x and projected by k_proj / v_proj;
+    no RoPE and no mask; fp32 scores and softmax, probabilities cast to the
+    working dtype, fp32 P.V cast back.  ``p`` uses the reference keys
+    (Wq, Wk, Wv, Wo, W_gate, W_up, W_down, W_norm_1, W_norm_2)."""
+    x = _c(x, dt)
+    context = _c(context, dt)
+    residual = x
+    xn = rms_norm(x, p["W_norm_1"], cfg.eps, dt)
+    cn = rms_norm(context, p["W_norm_1"], cfg.eps, dt)
+    B, L, _ = xn.shape
+    Lc = cn.shape[1]
+    D = cfg.head_dim
+    q = linear(xn, p["Wq"], dt=dt).view(B, L, cfg.heads, D)
+    k = linear(cn, p["Wk"], dt=dt).view(B, Lc, cfg.kv_heads, D)
+    v = linear(cn, p["Wv"], dt=dt).view(B, Lc, cfg.kv_heads, D)
+    ctx = attention(q, k, v, causal=False, dt=dt)
+    x = linear(ctx, p["Wo"], dt=dt) + residual
+    residual = x
+    h = rms_norm(x, p["W_norm_2"], cfg.eps, dt)
+    return swiglu_mlp(h, p, dt) + residual
+
+
+def llama_block_rope_cross(key, value, x, p, cfg, dt=F32):
+    """The Allo cross block (vla/llama_block_rope_bf16.py:617-709): Q = RoPE(RMSNorm(x) Wq),
+    the GIVEN key [B, L, kv_dim] is rotated by RoPE at positions 0..L-1 as well
+    (:629-630), the given value is used as is, the score is causally masked
+    (:641-652, the key sequence has the query's length), then the output
+    projection and the SwiGLU MLP with residuals.  Numerics follow the
+    reference's torch twin of this block (AttentionExpertBlock,
+    vla/llama_block_rope_bf16.py:60-131: RoPE evaluated and returned in fp32,
+    fp32 scores and softmax, probabilities and context in the working dtype), so
+    that with key = RMSNorm(x) Wk and value = RMSNorm(x) Wv it reproduces that
+    module exactly."""
+    x = _c(x, dt)
+    residual = x
+    h = rms_norm(x, p["W_norm_1"], cfg.eps, dt)
+    B, L, _ = h.shape
+    D = cfg.head_dim
+    q = apply_rope(linear(h, p["Wq"], dt=dt).view(B, L, cfg.heads, D), cfg.rope_theta, dt=dt)
+    k = apply_rope(_c(key, dt).view(B, L, cfg.kv_heads, D), cfg.rope_theta, dt=dt)
+    v = _c(value, dt).view(B, L, cfg.kv_heads, D)
+    ctx = attention(q, k, v, causal=True, dt=dt)
+    x = linear(ctx, p["Wo"], dt=dt) + residual
+    residual = x
+    h = rms_norm(x, p["W_norm_2"], cfg.eps, dt)
+    return swiglu_mlp(h, p, dt) + residual
+
+
 def time_embedding(t: float, dim: int, min_period: float, max_period: float) -> torch.Tensor:
     """Sinusoidal embedding of a scalar time: [sin(2 pi t / p_i), cos(2 pi t / p_i)],
     p_i log-spaced in [min_period, max_period], i < dim/2 (fp64 math, fp32 out)."""
@@ -282,10 +335,11 @@ def prefix_embed(image_tokens, token_ids, state, params, cfg, dt=F32):
     return torch.cat([_c(image_tokens, dt), _c(emb, dt), st], dim=1)
 
 
-def expert_velocity(x_t, t, text_kv, params, cfg, dt=F32):
+def expert_velocity(x_t, t, text_kv, params, cfg, dt=F32, kv_len=None):
     """v(x_t, t): in-projection + time embedding, expert layers (even: causal self,
-    odd: cross to that layer's projected prefix K/V), final RMSNorm, out-projection
-    (vla/vla.py:194-222 layer schedule and postprocessing)."""
+    odd: cross to that layer's projected prefix K/V, keys >= kv_len[b] masked),
+    final RMSNorm, out-projection (vla/vla.py:194-222 layer schedule and
+    postprocessing)."""
     e = cfg.expert
     temb = time_embedding(t, e.hidden, e.min_period, e.max_period)
     h = linear(x_t, params["W_action_in"], dt=dt) + _c(temb, dt)
@@ -294,7 +348,7 @@ def expert_velocity(x_t, t, text_kv, params, cfg, dt=F32):
             h = expert_self_block(h, lp, e, dt)
         else:
             kc, vc = text_kv[i]
-            h = expert_cross_block(h, kc, vc, lp, e, dt=dt)
+            h = expert_cross_block(h, kc, vc, lp, e, kv_len=kv_len, dt=dt)
     h = rms_norm(h, params["W_exp_norm"], e.eps, dt)
     return linear(h, params["W_action_out"], dt=dt)
 
@@ -309,11 +363,32 @@ def smolvla_chunk(obs, params, cfg, dt=F32):
         x, k, v = text_block(x, lp, cfg.text, dt)
         if i % 2 == 1 and i < cfg.expert.layers:
             text_kv[i] = expert_cross_kv(k, v, params["expert"][i], dt)
+    return flow_matching(obs["noise"], text_kv, params, cfg, dt)
+
+
+def flow_matching(noise, text_kv, params, cfg, dt=F32, kv_len=None):
+    """Euler integration of the action chunk from x0 = noise [B, chunk, action_dim]:
+    x_{k+1} = x_k + dt_k * v(x_k, t_k), t_k = 1 - k/steps, dt_k = -1/steps, the
+    state kept in fp32 (not in the reference, whose vla/vla.py:312 feeds noise
+    straight into one expert pass)."""
     e = cfg.expert
-    xt = obs["noise"].to(F32)
+    xt = noise.to(F32)
     step = -1.0 / e.steps
     for s in range(e.steps):
         t = 1.0 + s * step
-        vel = expert_velocity(xt.to(dt), t, text_kv, params, cfg, dt)
+        vel = expert_velocity(xt.to(dt), t, text_kv, params, cfg, dt, kv_len=kv_len)
         xt = xt + step * vel.to(F32)
     return xt
+
+
+def action_expert_chunk(noise, prefix_k, prefix_v, params, cfg, kv_len=None, dt=F32):
+    """The action expert on its own (benchmark configuration C3): ``prefix_k`` /
+    ``prefix_v`` [layers, B, Lc, text kv_dim] are a cached VLM prefix K/V per text
+    layer; each cross layer i projects layer i's K/V by its Wk_cross / Wv_cross
+    (vla/action_expert_bf16.py:756-759) and attends to it with keys >= kv_len[b]
+    masked; 10 Euler steps as in flow_matching."""
+    text_kv = {}
+    for i, lp in enumerate(params["expert"]):
+        if i % 2 == 1:
+            text_kv[i] = expert_cross_kv(_c(prefix_k[i], dt), _c(prefix_v[i], dt), lp, dt)
+    return flow_matching(noise, text_kv, params, cfg, dt, kv_len=kv_len)

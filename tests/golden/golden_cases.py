@@ -14,10 +14,12 @@ from vla_b200.configs import ExpertCfg, TextCfg, VisionCfg
 
 TEXT_CONSTS = dict(SEQ=24, EMBD=192, Q_H=6, KV_H=2, HEAD_DIM=64, FFN_HID=320, BATCH=1)
 EXP_CONSTS = dict(SEQ=20, TEXT_SEQ=24, EMBD=144, Q_H=6, KV_H=2, HEAD_DIM=64, KV_DIM=128, FFN_HID=256, BATCH=1)
+LLAMA_CONSTS = dict(SEQ=20, EMBD=128, Q_H=6, KV_H=2, HEAD_DIM=64, FFN_HID=512, BATCH=1)
 VIT_CONSTS = dict(SEQ=40, EMBD=128, N_HEAD=2, HEAD_DIM=64, FFN_HID=512, BATCH=1)
 
 TEXT_CFG = TextCfg(hidden=192, heads=6, kv_heads=2, head_dim=64, ffn=320)
 EXP_CFG = ExpertCfg(hidden=144, heads=6, kv_heads=2, head_dim=64, ffn=256)
+LLAMA_CFG = TextCfg(hidden=128, heads=6, kv_heads=2, head_dim=64, ffn=512, eps=1e-5, rope_theta=1e4)
 VIT_CFG = VisionCfg(hidden=128, heads=2, head_dim=64, ffn=512)
 
 CASES = {
@@ -28,6 +30,10 @@ CASES = {
     "exp_self": dict(kind="expert_self", consts=EXP_CONSTS, patch={"ln_1.eps": 1e-5, "ln_2.eps": 1e-5}),
     "exp_cross": dict(kind="expert_cross", consts=EXP_CONSTS, patch={"ln_1.eps": 1e-5, "ln_2.eps": 1e-5}),
     "minivit": dict(kind="minivit", consts=VIT_CONSTS),
+    # vla/llama_block_rope_bf16.py: the torch twin of llama_block_rope (AttentionExpertBlock)
+    # and the external-context block (CrossAttentionBlock)
+    "llama_rope": dict(kind="llama_rope", consts=LLAMA_CONSTS, patch={"ln_1.eps": 1e-5, "ln_2.eps": 1e-5}),
+    "cross_attn": dict(kind="cross_attn", consts=LLAMA_CONSTS, patch={"ln_1.eps": 1e-5, "ln_2.eps": 1e-5}),
     "siglip_emb": dict(kind="siglip_emb", consts=dict(EMBED=128, IMAGE=64, PATCH=16)),
     "con_ref": dict(kind="con_ref", consts={}),
     "masked_softmax_cpu": dict(kind="masked_softmax_cpu", consts=dict(SEQ=32)),
@@ -55,6 +61,14 @@ def case_inputs(name: str) -> dict:
         tk = W.randn((1, c["TEXT_SEQ"], c["KV_DIM"]), SEED, "golden.exp.tk", dtype=torch.float32)
         tv = W.randn((1, c["TEXT_SEQ"], c["KV_DIM"]), SEED, "golden.exp.tv", dtype=torch.float32)
         return {"params": p, "args": [x, tk, tv]}
+    if kind in ("llama_rope", "cross_attn"):
+        c = LLAMA_CONSTS
+        p = W.text_block_params(LLAMA_CFG, seed=SEED, layer=7)
+        x = W.randn((1, c["SEQ"], c["EMBD"]), SEED, "golden.llama.x", dtype=torch.float32)
+        if kind == "llama_rope":
+            return {"params": p, "args": [x]}
+        ctx = W.randn((1, 24, c["EMBD"]), SEED, "golden.llama.ctx", dtype=torch.float32)
+        return {"params": p, "args": [x, ctx]}
     if kind == "minivit":
         c = VIT_CONSTS
         p = W.vision_block_params(VIT_CFG, seed=SEED)

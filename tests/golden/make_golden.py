@@ -10,6 +10,8 @@ supplies their module-level constants:
   ActionExpertSelfBlock     vla/action_expert_bf16.py:69-131
   ActionExpertCrossBlock    vla/action_expert_bf16.py:137-207
   masked_softmax_cpu        vla/action_expert_bf16.py:530-538
+  AttentionExpertBlock      vla/llama_block_rope_bf16.py:60-131
+  CrossAttentionBlock       vla/llama_block_rope_bf16.py:133-180
   MiniVit                   vla/vision_block_bf16.py:57-79
   SiglipVisionConfig/Embeddings  vla/vit_emb.py:19-47
   con_ref                   vla/vla.py:434-437
@@ -103,6 +105,16 @@ def run(ref_root: str) -> dict:
             _set_linear(m.o_proj, p["Wo"]); _set_linear(m.gate_proj, p["W_gate"])
             _set_linear(m.up_proj, p["W_up"]); _set_linear(m.down_proj, p["W_down"])
             m.ln_1.weight.data = p["W_norm_1"].float(); m.ln_2.weight.data = p["W_norm_2"].float()
+        elif kind in ("llama_rope", "cross_attn"):
+            cls = "AttentionExpertBlock" if kind == "llama_rope" else "CrossAttentionBlock"
+            ns = load_defs(os.path.join(ref_root, "vla/llama_block_rope_bf16.py"), [cls], c)
+            m = ns[cls]().eval()
+            a = m.attn if kind == "llama_rope" else m
+            _set_linear(a.q_proj, p["Wq"]); _set_linear(a.k_proj, p["Wk"]); _set_linear(a.v_proj, p["Wv"])
+            _set_linear(m.attn.output_proj if kind == "llama_rope" else m.o_proj, p["Wo"])
+            _set_linear(m.gate_proj, p["W_gate"]); _set_linear(m.up_proj, p["W_up"])
+            _set_linear(m.down_proj, p["W_down"])
+            m.ln_1.weight.data = p["W_norm_1"].float(); m.ln_2.weight.data = p["W_norm_2"].float()
         elif kind == "minivit":
             ns = load_defs(os.path.join(ref_root, "vla/vision_block_bf16.py"), ["MiniVit"], c)
             torch.manual_seed(0)
@@ -149,7 +161,8 @@ def run(ref_root: str) -> dict:
 
         # TextEncoderBlock / ActionExpert*Block hard-cast the attention context to
         # bf16 (vla/text_encoder_bf16.py:126), so they only run as bf16 modules.
-        dts = (("bf16", torch.bfloat16),) if kind in ("text", "expert_self", "expert_cross") else (
+        dts = (("bf16", torch.bfloat16),) if kind in ("text", "expert_self", "expert_cross", "llama_rope",
+                                                      "cross_attn") else (
             ("f32", torch.float32), ("bf16", torch.bfloat16))
         for dt_name, dt in dts:
             mm = m.to(dt)

@@ -84,3 +84,72 @@ def test_workspace_query():
     n_without = _lib.load().vla_llama_layer_workspace(ctypes.byref(s), 113, 0)
     assert n_with - n_without >= 113 * 1600 * 2
     assert n_without >= 113 * (960 + 960 + 2560) * 2
+
+
+def test_layer_row_count_bounded_before_size_arithmetic():
+    """batch * seq at or above 2^31 rows is rejected before any workspace size is
+    computed or any kernel launched (the size products would otherwise wrap)."""
+    lib = _lib.load()
+    s = _lib.LlamaLayer()
+    s.norm1 = s.w_qkv = s.w_o = s.norm2 = s.w_gu = s.w_down = 256
+    s.hidden, s.heads, s.kv_heads, s.head_dim, s.ffn, s.eps = 960, 15, 5, 64, 2560, 1e-5
+    assert lib.vla_llama_layer_workspace(ctypes.byref(s), 1 << 31, 1) == 2 ** 64 - 1
+    before = lib.vla_launch_count()
+    big = 1 << 20
+    rc = lib.vla_llama_self_layer_bf16(ctypes.byref(s), ctypes.c_void_p(256), big, big, ctypes.c_void_p(256), None,
+                                       ctypes.c_void_p(256), 2 ** 63, None)
+    assert rc == _lib.VLA_E_INVALID and "2^31" in _lib.last_error()
+    rc = lib.vla_llama_cross_layer_bf16(ctypes.byref(s), ctypes.c_void_p(256), big, big, ctypes.c_void_p(256),
+                                        ctypes.c_void_p(256), ctypes.c_void_p(256), 320, 113, None,
+                                        ctypes.c_void_p(256), 2 ** 63, None)
+    assert rc == _lib.VLA_E_INVALID and "2^31" in _lib.last_error()
+    rc = lib.vla_llama_self_layer_bf16_noalloc(ctypes.byref(s), ctypes.c_void_p(256), big, big,
+                                               ctypes.c_void_p(256), None, None)
+    assert rc == _lib.VLA_E_INVALID and "2^31" in _lib.last_error()
+    assert lib.vla_launch_count() == before
+
+
+def test_expired_wait_rejects_bad_limits():
+    lib = _lib.load()
+    assert lib.vla_test_expired_wait(0, None) == _lib.VLA_E_INVALID
+    assert lib.vla_test_expired_wait(2_000_000, None) == _lib.VLA_E_INVALID
+
+
+def test_weight_cache_follows_in_place_refills():
+    """Device copies of reference params are reused while the host array is
+    unchanged and refreshed when the caller refills it in place (numpy and torch)."""
+    import numpy as np
+    from vla_b200._host import _Cache, fingerprint
+    a = np.arange(12, dtype=np.float32).reshape(3, 4)
+    f0 = fingerprint(a)
+    a[1, 2] = -1.0
+    assert fingerprint(a) != f0
+    t = torch.zeros(3, 4)
+    g0 = fingerprint(t)
+    t.add_(1.0)
+    assert fingerprint(t) != g0
+    # the cache's own behaviour, with a CPU "device copy"
+    c = _Cache()
+    made = []
+
+    def make(src):
+        made.append(1)
+        return torch.as_tensor(np.array(src, copy=True))
+
+    orig = torch.cuda.current_device
+    torch.cuda.current_device = lambda: 0
+    try:
+        x1 = c.get(a, "t", lambda: make(a))
+        x2 = c.get(a, "t", lambda: make(a))
+        assert x1 is x2 and len(made) == 1
+        a[0, 0] = 42.0
+        x3 = c.get(a, "t", lambda: make(a))
+        assert len(made) == 2 and float(x3[0, 0]) == 42.0
+        # composite sources: a change in any of them refreshes the entry
+        b = np.ones(4, dtype=np.float32)
+        c.get((a, b), "cat", lambda: make(b))
+        b[0] = 5.0
+        c.get((a, b), "cat", lambda: make(b))
+        assert len(made) == 4
+    finally:
+        torch.cuda.current_device = orig

@@ -12,7 +12,7 @@ from vla_b200.configs import VisionCfg
 
 import sys
 sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
-from golden_cases import EXP_CFG, TEXT_CFG, VIT_CFG, case_inputs  # noqa: E402
+from golden_cases import EXP_CFG, LLAMA_CFG, TEXT_CFG, VIT_CFG, case_inputs  # noqa: E402
 
 GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_oracle.npz"))
 BF = torch.bfloat16
@@ -98,3 +98,32 @@ def test_masked_softmax_cpu():
     s = s.masked_fill(torch.ones(L, L).triu(1).bool(), float("-inf"))
     p = torch.softmax(s, dim=-1).to(BF)
     _cmp(p, "masked_softmax_cpu", atol=0, rtol=0)
+
+
+def test_llama_block_rope_self():
+    """AttentionExpertBlock (vla/llama_block_rope_bf16.py:60-131), the torch twin of
+    llama_block_rope, against the oracle's text block with its hyper-parameters."""
+    inp = case_inputs("llama_rope")
+    out, _, _ = R.text_block(inp["args"][0], inp["params"], LLAMA_CFG, dt=BF)
+    _cmp(out, "llama_rope.bf16")
+
+
+def test_llama_block_rope_cross_pinned_by_self_block():
+    """The Allo cross path (vla/llama_block_rope_bf16.py:617-709) given key =
+    RMSNorm(x) Wk before RoPE and value = RMSNorm(x) Wv computes exactly the self
+    block, so the reference's AttentionExpertBlock output pins the restatement."""
+    inp = case_inputs("llama_rope")
+    x, p = inp["args"][0], inp["params"]
+    h = R.rms_norm(x.to(BF), p["W_norm_1"], LLAMA_CFG.eps, BF)
+    key, value = R.linear(h, p["Wk"], dt=BF), R.linear(h, p["Wv"], dt=BF)
+    out = R.llama_block_rope_cross(key, value, x, p, LLAMA_CFG, dt=BF)
+    _cmp(out, "llama_rope.bf16")
+
+
+def test_cross_attention_block():
+    """CrossAttentionBlock (vla/llama_block_rope_bf16.py:133-180): context through
+    ln_1 and k_proj / v_proj, no RoPE, no mask."""
+    inp = case_inputs("cross_attn")
+    x, ctx = inp["args"]
+    out = R.cross_attention_block(x, ctx, inp["params"], LLAMA_CFG, dt=BF)
+    _cmp(out, "cross_attn.bf16")

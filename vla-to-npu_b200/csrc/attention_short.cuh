@@ -199,8 +199,8 @@ __global__ void __launch_bounds__(kThreads, 4) attn_short_kernel(Params p) {
       tc_commit(&sm.bar);
     }
     ok = mbar_wait_bounded(&sm.bar, phase, &sm.abort);
+    if (!ok) *(volatile int*)&sm.abort = 1;  // the other warps stop waiting at once
     phase ^= 1u;
-    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
 
     // softmax of this thread's row
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 4) attn_short_kernel(Params p) {
       tmem_st32u(srow + 32 * h, pk);
     }
     tc_fence_before();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;  // one verdict for the whole block
     tc_fence_after();
 
     // O = P V
@@ -247,8 +247,8 @@ __global__ void __launch_bounds__(kThreads, 4) attn_short_kernel(Params p) {
       tc_commit(&sm.bar);
     }
     ok = ok && mbar_wait_bounded(&sm.bar, phase, &sm.abort);
+    if (!ok) *(volatile int*)&sm.abort = 1;
     phase ^= 1u;
-    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
 
     // O row / l into the Q tile (row r at r * 128 bytes, 16-byte chunks swizzled
@@ -284,16 +284,15 @@ __global__ void __launch_bounds__(kThreads, 4) attn_short_kernel(Params p) {
         }
       }
     }
-    // the next item's copies overwrite the tiles and its MMA the TMEM columns
+    // the next item's copies overwrite the tiles and its MMA the TMEM columns;
+    // the barrier also makes `ok` block-uniform, so every warp leaves the loop
+    // on the same iteration
     tc_fence_before();
-    __syncthreads();
+    ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-  if (!ok && threadIdx.x == 0) {
-    if (!sm.abort) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
-    sm.abort = 1;
-  }
+  if (!ok && threadIdx.x == 0) vla_record_error(VLA_DERR_ATTN_TIMEOUT);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -64,12 +64,6 @@ constexpr uint32_t S_COL0 = 0;    // S_0, S_1 at columns 0 and 128
 constexpr uint32_t P_COL0 = 256;  // P_0, P_1 (bf16 pairs) at columns 256 and 320
 constexpr uint32_t O_COL0 = 384;  // O_0, O_1 at columns 384 and 448
 constexpr float kRescaleLog2 = 8.f;
-// One key pair in kPolyPeriod has its exponentials evaluated by ex2_poly
-// instead of MUFU.EX2 (0 = none).
-#ifndef VLA_ATTN_POLY_PERIOD
-#define VLA_ATTN_POLY_PERIOD 0
-#endif
-constexpr int kPolyPeriod = VLA_ATTN_POLY_PERIOD;
 
 struct Params {
   int Lq, Lk, Hq, Hkv, batch;
@@ -99,22 +93,6 @@ __device__ __forceinline__ float ex2_fast(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA and integer pipes, for part of the exponentials (MUFU.EX2
-// issues 16 lanes per clock per SM, the FMA pipe 128): Cody-Waite split
-// x = j + f with j = floor(x) from a round-down add of 1.5 * 2^23, f in [0, 1),
-// 2^f from a cubic minimax fit (coefficients fitted for this kernel; relative
-// error below 7.5e-5, far under the 2^-9 rounding of the bf16 P it feeds), and
-// j added to the exponent field.  x is clamped at -127 (masked keys give
-// 2^-127, which is negligible next to the row maximum's 2^0 .. 2^8).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -127.f);
-  const float r = __fadd_rd(x, 12582912.f);  // 1.5 * 2^23 + floor(x), exact
-  const float f = x - (r - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.07802452f, f, 0.22606716f), f, 0.69583356f), f, 0.99992520f);
-  const int j = __float_as_int(r) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (j << 23));
 }
 
 // Packed fp32 pairs (one instruction for two lanes' worth of FMA-pipe work):
@@ -517,9 +495,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BKV; c += 2) {
           float x0, x1;
           fma2(sr[c], sr[c + 1], p.scale_log2, -mbase, x0, x1);
-          const bool poly = kPolyPeriod > 0 && ((c >> 1) % (kPolyPeriod > 0 ? kPolyPeriod : 1)) == 0;
-          const float e0 = poly ? ex2_poly(x0) : ex2_fast(x0);
-          const float e1 = poly ? ex2_poly(x1) : ex2_fast(x1);
+          const float e0 = ex2_fast(x0);
+          const float e1 = ex2_fast(x1);
           if (c < 8) {
             rs8[c & 7] = e0;
             rs8[(c + 1) & 7] = e1;

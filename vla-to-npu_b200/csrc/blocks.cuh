@@ -182,7 +182,14 @@ struct LlamaWs {
   bf16 *h, *qkv, *attn, *mlp;
 };
 
+// Layer calls take rows = batch * seq below 2^31 (the GEMM's M limit); checking
+// it before any size arithmetic keeps the workspace products far from int64
+// overflow (rows * width * 2 < 2^31 * 2^32).
+static constexpr int64_t kMaxLayerRows = (1ll << 31) - 1;
+
 static size_t llama_ws_bytes(const vla_llama_layer* w, int64_t rows, bool need_qkv) {
+  if (rows < 0 || rows > kMaxLayerRows || w->hidden < 0 || w->ffn < 0 || w->heads < 0 || w->kv_heads < 0)
+    return SIZE_MAX;
   const int64_t q = (int64_t)w->heads * w->head_dim, kv = (int64_t)w->kv_heads * w->head_dim;
   size_t s = align_up(rows * w->hidden * 2) + align_up(rows * q * 2) + align_up(rows * w->ffn * 2);
   if (need_qkv) s += align_up(rows * (q + 2 * kv) * 2);
@@ -233,6 +240,7 @@ static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, co
   if (rc) return rc;
   VLA_CHECK_ARG(xv && rope_cs && batch >= 0 && seq > 0, "llama self: bad arguments");
   const int64_t rows = (int64_t)batch * seq;
+  VLA_CHECK_ARG(rows <= kMaxLayerRows, "llama self: batch * seq = %lld rows, above 2^31 - 1", (long long)rows);
   const bool own_qkv = qkv_out == nullptr;
   VLA_CHECK_ARG(ws != nullptr || rows == 0, "llama self: null workspace");
   if (ws_bytes < llama_ws_bytes(w, rows, own_qkv))
@@ -284,6 +292,7 @@ static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, c
   if (rc) return rc;
   VLA_CHECK_ARG(xv && rope_cs && k && v && batch >= 0 && seq > 0 && kv_seq >= 0, "llama cross: bad arguments");
   const int64_t rows = (int64_t)batch * seq;
+  VLA_CHECK_ARG(rows <= kMaxLayerRows, "llama cross: batch * seq = %lld rows, above 2^31 - 1", (long long)rows);
   const int64_t H = w->hidden, Q = (int64_t)w->heads * 64;
   VLA_CHECK_ARG(ldkv >= (int64_t)w->kv_heads * 64, "llama cross: ldkv too small");
   if (ws_bytes < llama_ws_bytes(w, rows, true))
@@ -335,6 +344,7 @@ static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, c
 // SigLIP encoder layer
 // ----------------------------------------------------------------------------
 static size_t vision_ws_bytes(const vla_vision_layer* w, int64_t rows) {
+  if (rows < 0 || rows > kMaxLayerRows || w->hidden < 0 || w->ffn < 0) return SIZE_MAX;
   const int64_t H = w->hidden;
   return align_up(rows * H * 2) + align_up(rows * 3 * H * 2) + align_up(rows * H * 2) + align_up(rows * w->ffn * 2);
 }
@@ -346,7 +356,9 @@ static int vision_layer(const vla_vision_layer* w, void* xv, int batch, int seq,
                     w->w_fc1 && w->b_fc1 && w->w_fc2 && w->b_fc2,
                 "vision layer: null weight");
   VLA_CHECK_ARG(w->head_dim == 64 && w->heads * 64 == w->hidden, "vision layer: heads * 64 must equal hidden");
+  VLA_CHECK_ARG(batch >= 0 && seq > 0, "vision layer: bad batch / seq");
   const int64_t rows = (int64_t)batch * seq, H = w->hidden, F = w->ffn;
+  VLA_CHECK_ARG(rows <= kMaxLayerRows, "vision layer: batch * seq = %lld rows, above 2^31 - 1", (long long)rows);
   if (ws_bytes < vision_ws_bytes(w, rows))
     return set_error(VLA_E_WORKSPACE, "vision layer: workspace %zu < %zu", ws_bytes, vision_ws_bytes(w, rows));
   VLA_CHECK_ALIGN(aligned16(ws) && aligned16(xv), "vision layer: alignment");

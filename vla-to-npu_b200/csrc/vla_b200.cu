@@ -40,9 +40,25 @@ static void* noalloc_scratch(int* rc) {
   return addr[dev];
 }
 
+// One thread waits on a fresh mbarrier that nothing arrives on; the bounded
+// wait gives up after limit_ns and records the test code.
+__global__ void expired_wait_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  if (!mbar_wait_bounded(&bar, 0u, nullptr, limit_ns)) vla_record_error(VLA_DERR_TEST_TIMEOUT);
+}
+
 extern "C" {
 
 const char* vla_last_error(void) { return t_last_error; }
+
+int vla_test_expired_wait(int32_t limit_us, vla_stream_t stream) {
+  VLA_CHECK_ARG(limit_us >= 1 && limit_us <= 1000000, "test_expired_wait: limit_us must be in [1, 1e6]");
+  expired_wait_kernel<<<1, 32, 0, as_stream(stream)>>>((uint64_t)limit_us * 1000ull);
+  return launch_status("test_expired_wait");
+}
 
 int vla_version(void) { return 100; }
 
@@ -310,6 +326,8 @@ int vla_llama_self_layer_bf16_noalloc(const vla_llama_layer* w, void* x, int32_t
                                       const float* rope_cs, void* qkv_out, vla_stream_t stream) {
   VLA_CHECK_ARG(w != nullptr && batch >= 0 && seq > 0, "noalloc llama self: bad arguments");
   const int64_t rows = (int64_t)batch * seq;
+  VLA_CHECK_ARG(rows <= blocks::kMaxLayerRows, "noalloc llama self: batch * seq = %lld rows, above 2^31 - 1",
+                (long long)rows);
   const size_t need = blocks::llama_ws_bytes(w, rows, qkv_out == nullptr);
   if (need > VLA_NOALLOC_SCRATCH_BYTES)
     return set_error(VLA_E_WORKSPACE,

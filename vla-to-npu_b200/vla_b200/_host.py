@@ -3,13 +3,15 @@
 The reference's block builders and per-op harnesses take numpy arrays
 (``ml_dtypes.bfloat16`` or float32) and return numpy bf16 arrays, with
 weights in a ``params`` dict ([in, out] layout).  These helpers move such
-arrays to the GPU (caching uploaded weights by identity, so that calling a
-block repeatedly with the same ``params`` uploads them once) and bring
+arrays to the GPU (caching uploaded weights by identity and content, so that
+calling a block repeatedly with the same ``params`` uploads them once, and a
+params array refilled in place is uploaded again) and bring
 results back in the caller's array type.
 """
 from __future__ import annotations
 
 import weakref
+import zlib
 from typing import Any, Callable, Dict, Tuple
 
 import numpy as np
@@ -44,23 +46,46 @@ def to_host_like(t: torch.Tensor, like) -> Any:
     return t.detach().cpu()
 
 
+def fingerprint(obj) -> Tuple:
+    """What identifies the CONTENT of a host weight: a torch tensor's storage
+    pointer and in-place version counter (torch bumps ``_version`` on every
+    in-place write), a numpy array's CRC-32 over its bytes, nothing for other
+    objects (tables keyed by a function or module)."""
+    if isinstance(obj, torch.Tensor):
+        return ("torch", obj.data_ptr(), obj._version, tuple(obj.shape), str(obj.dtype))
+    if isinstance(obj, np.ndarray):
+        a = np.ascontiguousarray(obj)
+        return ("numpy", zlib.crc32(a.view(np.uint8).reshape(-1).data), a.shape, a.dtype.str)
+    return ()
+
+
 class _Cache:
-    """Device copies of host weights keyed by (id, shape, transform); entries die with
-    their host array when it is weak-referenceable, else live for the process."""
+    """Device copies of host weights.  An entry is found by the identity of its
+    source array(s) and the transform's tag, and is reused only while the
+    sources' content fingerprints are unchanged: refilling a params array in
+    place (numpy or torch) makes the next call upload it again.  Entries die
+    with their host arrays when those are weak-referenceable."""
 
     def __init__(self):
-        self._d: Dict[Tuple, torch.Tensor] = {}
+        self._d: Dict[Tuple, Tuple[Tuple, torch.Tensor]] = {}
 
-    def get(self, key_obj, tag: str, make: Callable[[], torch.Tensor]) -> torch.Tensor:
-        key = (id(key_obj), tag, getattr(key_obj, "shape", None), torch.cuda.current_device())
-        t = self._d.get(key)
-        if t is None:
-            t = make()
-            self._d[key] = t
-            try:
-                weakref.finalize(key_obj, self._d.pop, key, None)
-            except TypeError:
-                pass
+    def get(self, sources, tag: str, make: Callable[[], torch.Tensor]) -> torch.Tensor:
+        srcs = sources if isinstance(sources, tuple) else (sources,)
+        key = (tuple(id(o) for o in srcs), tag, tuple(getattr(o, "shape", None) for o in srcs),
+               torch.cuda.current_device())
+        fp = tuple(fingerprint(o) for o in srcs)
+        hit = self._d.get(key)
+        if hit is not None and hit[0] == fp:
+            return hit[1]
+        t = make()
+        fresh = hit is None
+        self._d[key] = (fp, t)
+        if fresh:
+            for o in srcs:
+                try:
+                    weakref.finalize(o, self._d.pop, key, None)
+                except TypeError:
+                    pass
         return t
 
 

@@ -32,10 +32,10 @@ def llama_layer(params: Dict, eps: float, cross: bool = False) -> Tuple[_lib.Lla
         kv_dim = params["Wk_cross"].shape[1]
     else:
         kv_dim = params["Wk"].shape[1]
-        w_qkv = WEIGHTS.get(params["Wq"], "qkv_self", lambda: torch.cat(
+        w_qkv = WEIGHTS.get((params["Wq"], params["Wk"], params["Wv"]), "qkv_self", lambda: torch.cat(
             [to_device(params["Wq"]), to_device(params["Wk"]), to_device(params["Wv"])], dim=1).t().contiguous())
     w_o = weight_kmajor(params["Wo"])
-    w_gu = WEIGHTS.get(params["W_gate"], "gate_up", lambda: interleave_gate_up(
+    w_gu = WEIGHTS.get((params["W_gate"], params["W_up"]), "gate_up", lambda: interleave_gate_up(
         to_device(params["W_gate"]), to_device(params["W_up"]), "cuda"))
     w_down = weight_kmajor(params["W_down"])
     n1, n2 = vector(params["W_norm_1"]), vector(params["W_norm_2"])
@@ -56,13 +56,15 @@ def vision_layer(params: Dict, eps: float) -> Tuple[_lib.VisionLayer, list]:
     F = params["W_up"].shape[1]
     zeros_h = WEIGHTS.get(torch, f"zeros:{H}", lambda: torch.zeros(H, dtype=BF16, device="cuda"))
     zeros_f = WEIGHTS.get(torch, f"zeros:{F}", lambda: torch.zeros(F, dtype=BF16, device="cuda"))
-    w_qkv = WEIGHTS.get(params["Wq"], "qkv_vision", lambda: torch.cat(
+    w_qkv = WEIGHTS.get((params["Wq"], params["Wk"], params["Wv"]), "qkv_vision", lambda: torch.cat(
         [to_device(params["Wq"]), to_device(params["Wk"]), to_device(params["Wv"])], dim=1).t().contiguous())
 
     def bias(key, z):
         return vector(params[key]) if key in params else z
 
-    b_qkv = WEIGHTS.get(params["Wq"], "bqkv_vision", lambda: torch.cat(
+    bsrc = tuple(params[k] for k in ("bq", "bk", "bv") if k in params)
+    b_tag = f"bqkv_vision:{H}:" + ",".join(k for k in ("bq", "bk", "bv") if k in params)
+    b_qkv = WEIGHTS.get(bsrc + (torch,), b_tag, lambda: torch.cat(
         [bias("bq", zeros_h), bias("bk", zeros_h), bias("bv", zeros_h)]).contiguous())
     keep = [w_qkv, b_qkv, weight_kmajor(params["Wo"]), bias("bo", zeros_h), weight_kmajor(params["W_up"]),
             bias("b_up", zeros_f), weight_kmajor(params["W_down"]), bias("b_down", zeros_h),

@@ -51,7 +51,7 @@ def llama_block_rope_cross(key, value, x_np, params, *, rope_theta: float = 10_0
     # MLP half: x += down(silu(gate(rms(x))) * up(rms(x)))
     h = dev.rms_norm(x, vector(params["W_norm_2"]), eps)
     mid = torch.empty(seq, F, dtype=BF16, device=x.device)
-    w_gu = WEIGHTS.get(params["W_gate"], "gate_up", lambda: interleave_gate_up(
+    w_gu = WEIGHTS.get((params["W_gate"], params["W_up"]), "gate_up", lambda: interleave_gate_up(
         to_device(params["W_gate"]), to_device(params["W_up"]), "cuda"))
     dev.gemm(h, w_gu, mid, dev.make_epilogue(act=_lib.ACT_SWIGLU))
     dev.gemm(mid, weight_kmajor(params["W_down"]), x, dev.make_epilogue(residual=x))

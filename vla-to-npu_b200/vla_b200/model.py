@@ -122,6 +122,108 @@ class VisionLayerWeights:
 
 
 # ---------------------------------------------------------------------------
+# the action expert (benchmark configuration C3; the last stage of the model)
+# ---------------------------------------------------------------------------
+class ActionExpert:
+    """The 16-layer action expert with its flow-matching loop, on the device.
+
+    Even layers: causal self-attention over the chunk; odd layers: cross-attention
+    to a cached prefix K/V (the K/V of text layer i, projected once per chunk by
+    layer i's Wk_cross / Wv_cross and reused by every Euler step; the reference
+    recomputes the projection on every call, vla/action_expert_bf16.py:756-759).
+    ``kv_len`` (device int32 [B], optional) masks prefix keys >= kv_len[b]
+    (key padding).  Flow matching: x_{k+1} = x_k + dt v(x_k, t_k) with the fp32
+    state updated by the out-projection GEMM's epilogue."""
+
+    def __init__(self, cfg: SmolVLACfg, params: dict, device, ws: Optional[dev.Workspace] = None):
+        e = cfg.expert
+        d = torch.device(device)
+        self.cfg, self.device = cfg, d
+        self.layers = [LlamaLayerWeights(p, e, d, cross=(i % 2 == 1)) for i, p in enumerate(params["expert"])]
+        self.w_in = _kmajor(params["W_action_in"], d)
+        self.exp_norm = params["W_exp_norm"].to(BF16).contiguous().to(d)
+        self.w_out = _kmajor(params["W_action_out"], d)
+        self.temb = time_embedding_table(e).to(BF16).to(d)
+        self.rope = rope_table(e.chunk, e.head_dim, e.rope_theta).to(d)
+        self.ws = ws if ws is not None else dev.Workspace(d)
+        self.cross_index = {}
+        for i, lw in enumerate(self.layers):
+            if lw.cross:
+                self.cross_index[i] = len(self.cross_index)
+        self.batch = 0
+        self.prefix_len = 0
+        self.kv_len: Optional[torch.Tensor] = None
+
+    def allocate(self, batch: int, prefix_len: int) -> None:
+        if (batch, prefix_len) == (self.batch, self.prefix_len):
+            return
+        e, d = self.cfg.expert, self.device
+        self.batch, self.prefix_len = batch, prefix_len
+        rows_e = batch * e.chunk
+        self.kv_cross = torch.empty(len(self.cross_index), batch * prefix_len, 2 * e.kv_dim, dtype=BF16, device=d)
+        self.x_t = torch.empty(rows_e, e.action_dim, dtype=torch.float32, device=d)
+        self.x_b = torch.empty(rows_e, e.action_dim, dtype=BF16, device=d)
+        self.h = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
+        self.hn = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
+        self.kv_len_buf = torch.full((batch,), prefix_len, dtype=torch.int32, device=d)
+        lib = _lib.load()
+        import ctypes
+        self.ws.get(max(lib.vla_llama_layer_workspace(ctypes.byref(w.struct), rows_e, 1) for w in self.layers))
+
+    def project_prefix_kv(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Cross layer ``layer``'s K/V from the prefix K/V [B * prefix_len, text kv_dim]."""
+        e = self.cfg.expert
+        lw = self.layers[layer]
+        kvc = self.kv_cross[self.cross_index[layer]]
+        dev.gemm(k, lw.wk_cross, kvc[:, :e.kv_dim])
+        dev.gemm(v, lw.wv_cross, kvc[:, e.kv_dim:])
+
+    def set_kv_len(self, kv_len: Optional[torch.Tensor]) -> None:
+        """Key-padding lengths per observation (None: every prefix key is valid).
+        The values are copied into a fixed device buffer, so a captured graph
+        picks up new lengths on replay."""
+        if kv_len is None:
+            self.kv_len = None
+            return
+        self.kv_len_buf.copy_(kv_len.to(torch.int32), non_blocking=True)
+        self.kv_len = self.kv_len_buf
+
+    def run(self) -> torch.Tensor:
+        """The Euler loop from the noise already in ``x_t``; returns x_t [B * chunk, action_dim]."""
+        e = self.cfg.expert
+        B = self.batch
+        dev.f32_to_bf16(self.x_t, self.x_b)
+        dt = -1.0 / e.steps
+        for s in range(e.steps):
+            dev.gemm(self.x_b, self.w_in, self.h, dev.make_epilogue(bias=self.temb[s]))
+            for i, lw in enumerate(self.layers):
+                if lw.cross:
+                    kvc = self.kv_cross[self.cross_index[i]]
+                    dev.llama_cross_layer(lw.struct, self.h, B, e.chunk, self.rope, kvc[:, :e.kv_dim],
+                                          kvc[:, e.kv_dim:], self.prefix_len, self.ws, kv_len=self.kv_len)
+                else:
+                    dev.llama_self_layer(lw.struct, self.h, B, e.chunk, self.rope, self.ws)
+            dev.rms_norm(self.h, self.exp_norm, e.eps, out=self.hn)
+            dev.gemm(self.hn, self.w_out, self.x_b,
+                     dev.make_epilogue(act=_lib.ACT_EULER, euler_x=self.x_t, euler_dt=dt))
+        return self.x_t
+
+    def infer(self, noise: torch.Tensor, prefix_k: torch.Tensor, prefix_v: torch.Tensor,
+              kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Benchmark configuration C3: actions [B, chunk, action_dim] fp32 from the noise
+        [B, chunk, action_dim] and a cached prefix K/V [layers, B, prefix_len, text kv_dim]
+        per text layer (device tensors)."""
+        e = self.cfg.expert
+        B, Lc = noise.shape[0], prefix_k.shape[2]
+        self.allocate(B, Lc)
+        for i in self.cross_index:
+            self.project_prefix_kv(i, prefix_k[i].reshape(B * Lc, -1), prefix_v[i].reshape(B * Lc, -1))
+        self.set_kv_len(kv_len)
+        self.x_t.copy_(noise.reshape(B * e.chunk, -1))
+        return self.run().view(B, e.chunk, e.action_dim)
+
+
+# ---------------------------------------------------------------------------
 # the model
 # ---------------------------------------------------------------------------
 class SmolVLA:
@@ -144,14 +246,10 @@ class SmolVLA:
         self.embed_table = params["embed"].to(BF16).contiguous().to(d)
         self.w_state = _kmajor(params["W_state"], d)
         self.text = [LlamaLayerWeights(p, t, d) for p in params["text"]]
-        self.expert = [LlamaLayerWeights(p, e, d, cross=(i % 2 == 1)) for i, p in enumerate(params["expert"])]
-        self.w_in = _kmajor(params["W_action_in"], d)
-        self.exp_norm = params["W_exp_norm"].to(BF16).contiguous().to(d)
-        self.w_out = _kmajor(params["W_action_out"], d)
-        self.temb = time_embedding_table(e).to(BF16).to(d)
         self.rope_text = rope_table(pf.length, t.head_dim, t.rope_theta).to(d)
-        self.rope_exp = rope_table(e.chunk, e.head_dim, e.rope_theta).to(d)
         self.ws = dev.Workspace(d)
+        self.action = ActionExpert(cfg, params, d, self.ws)
+        self.expert = self.action.layers
         self.batch = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.graph_batch = 0
@@ -177,19 +275,13 @@ class SmolVLA:
         rows_t = B * pf.length
         self.prefix = torch.empty(rows_t, t.hidden, dtype=BF16, device=d)
         self.qkv = torch.empty(rows_t, t.q_dim + 2 * t.kv_dim, dtype=BF16, device=d)
-        n_cross = sum(1 for w in self.expert if w.cross)
-        self.kv_cross = torch.empty(n_cross, rows_t, 2 * e.kv_dim, dtype=BF16, device=d)
-        rows_e = B * e.chunk
-        self.x_t = torch.empty(rows_e, e.action_dim, dtype=torch.float32, device=d)
-        self.x_b = torch.empty(rows_e, e.action_dim, dtype=BF16, device=d)
-        self.h = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
-        self.hn = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
+        self.action.allocate(B, pf.length)
+        self.x_t = self.action.x_t
         lib = _lib.load()
         import ctypes
         need = max(
             lib.vla_vision_layer_workspace(ctypes.byref(self.vision[0].struct), rows_v) if self.vision else 0,
             lib.vla_llama_layer_workspace(ctypes.byref(self.text[0].struct), rows_t, 0),
-            max(lib.vla_llama_layer_workspace(ctypes.byref(w.struct), rows_e, 1) for w in self.expert),
         )
         self.ws.get(need)
         self.graph = None
@@ -220,39 +312,17 @@ class SmolVLA:
         dev.gemm(self.in_state, self.w_state, state_rows)
 
     def text_layers(self) -> None:
-        t, pf, e = self.cfg.text, self.cfg.prefix, self.cfg.expert
+        t, pf = self.cfg.text, self.cfg.prefix
         Q, KV = t.q_dim, t.kv_dim
-        ci = 0
         for i, lw in enumerate(self.text):
             dev.llama_self_layer(lw.struct, self.prefix, self.batch, pf.length, self.rope_text, self.ws,
                                  qkv_out=self.qkv)
             if i < len(self.expert) and self.expert[i].cross:
-                ew = self.expert[i]
-                kvc = self.kv_cross[ci]
-                dev.gemm(self.qkv[:, Q:Q + KV], ew.wk_cross, kvc[:, :e.kv_dim])
-                dev.gemm(self.qkv[:, Q + KV:Q + 2 * KV], ew.wv_cross, kvc[:, e.kv_dim:])
-                ci += 1
+                self.action.project_prefix_kv(i, self.qkv[:, Q:Q + KV], self.qkv[:, Q + KV:Q + 2 * KV])
 
     def action_expert(self) -> None:
-        e, pf = self.cfg.expert, self.cfg.prefix
-        B = self.batch
         self.x_t.copy_(self.in_noise)
-        dev.f32_to_bf16(self.x_t, self.x_b)
-        dt = -1.0 / e.steps
-        for s in range(e.steps):
-            dev.gemm(self.x_b, self.w_in, self.h, dev.make_epilogue(bias=self.temb[s]))
-            ci = 0
-            for lw in self.expert:
-                if lw.cross:
-                    kvc = self.kv_cross[ci]
-                    dev.llama_cross_layer(lw.struct, self.h, B, e.chunk, self.rope_exp, kvc[:, :e.kv_dim],
-                                          kvc[:, e.kv_dim:], pf.length, self.ws)
-                    ci += 1
-                else:
-                    dev.llama_self_layer(lw.struct, self.h, B, e.chunk, self.rope_exp, self.ws)
-            dev.rms_norm(self.h, self.exp_norm, e.eps, out=self.hn)
-            dev.gemm(self.hn, self.w_out, self.x_b,
-                     dev.make_epilogue(act=_lib.ACT_EULER, euler_x=self.x_t, euler_dt=dt))
+        self.action.run()
 
     def forward_device(self) -> torch.Tensor:
         """Launch the whole chunk forward on the current stream from the input buffers."""
