@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--ctas", type=int, default=0, choices=[0, 1, 2],
                     help="GEMM kernel cases: force one CTA (1) or a CTA pair (2) per tile; 0 = automatic")
     ap.add_argument("--tile-n", type=int, default=0, help="GEMM kernel cases: force the tile width BN; 0 = automatic")
+    ap.add_argument("--attn-impl", type=int, default=0,
+                    help="attention kernel cases: VLA_ATTN_* kernel choice (0 = automatic)")
     return ap.parse_args()
 
 
@@ -134,7 +136,7 @@ def run_kernel_case(args):
         fn = lambda: dev.attention(qkv[:, :Hq * 64], qkv[:, Hq * 64:(Hq + Hkv) * 64],  # noqa: E731
                                    qkv[:, (Hq + Hkv) * 64:], o, batch=B, Lq=L, Lk=L, Hq=Hq, Hkv=Hkv,
                                    q_batch=L * cols, k_batch=L * cols, v_batch=L * cols, o_batch=L * Hq * 64,
-                                   causal=True)
+                                   causal=True, impl=args.attn_impl)
         flops, nbytes = 4.0 * B * Hq * L * L * 64, 2.0 * B * L * (2 * Hq + 2 * Hkv) * 64
     elif name in ("attn_exp_self", "attn_exp_cross"):
         B, Lq, Hq, Hkv = 512, 50, 15, 5
@@ -151,7 +153,8 @@ def run_kernel_case(args):
             qb, kb = Lq * Hq * 64, Lk * 2 * Hkv * 64
         o = torch.empty(B * Lq, Hq * 64, dtype=bf, device="cuda")
         fn = lambda: dev.attention(q, k, v, o, batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=qb,  # noqa: E731
-                                   k_batch=kb, v_batch=kb, o_batch=Lq * Hq * 64, causal=name == "attn_exp_self")
+                                   k_batch=kb, v_batch=kb, o_batch=Lq * Hq * 64, causal=name == "attn_exp_self",
+                                   impl=args.attn_impl)
         flops, nbytes = 4.0 * B * Hq * Lq * Lk * 64, 2.0 * B * (2 * Lq * Hq + 2 * Lk * Hkv) * 64
     elif name == "rms_norm":
         x = W.randn((131072, 960), 0, "kc.x").cuda()

@@ -237,8 +237,18 @@ typedef struct vla_attention_args {
  * heads of a kv head stacked into 128-row tiles) for Lk <= 128, causal or not,
  * and the mma.sync kernel (64-row tiles) otherwise.  TCGEN05 supports
  * non-causal attention only and needs q_batch / k_batch / v_batch to be whole
- * multiples of the row strides; TCGEN05_SHORT needs Lk <= 128. */
-enum { VLA_ATTN_AUTO = 0, VLA_ATTN_MMA_SYNC = 1, VLA_ATTN_TCGEN05 = 2, VLA_ATTN_TCGEN05_SHORT = 3 };
+ * multiples of the row strides; TCGEN05_SHORT needs Lk <= 128.
+ * TCGEN05_PIPE is the pipelined short-sequence kernel (one warp-specialised
+ * CTA per SM, TMA loads and stores, per (sequence, kv head) items in flight
+ * while earlier items compute): 1 <= Lk <= 128, Lq <= 256,
+ * (Hq / Hkv) * Lq <= 512, and nonzero sequence strides when batch > 1. */
+enum {
+  VLA_ATTN_AUTO = 0,
+  VLA_ATTN_MMA_SYNC = 1,
+  VLA_ATTN_TCGEN05 = 2,
+  VLA_ATTN_TCGEN05_SHORT = 3,
+  VLA_ATTN_TCGEN05_PIPE = 4
+};
 int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream);
 
 /* Pixel shuffle: in [B, grid*grid, C] -> out [B, (grid/s)^2, s*s*C] with

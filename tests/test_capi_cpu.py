@@ -62,7 +62,7 @@ def test_host_validation_without_gpu():
     a.q_batch, a.k_batch, a.v_batch, a.o_batch = 960 * 50, 320 * 200, 320 * 200, 960 * 50
     a.batch, a.Lq, a.Lk, a.Hq, a.Hkv, a.head_dim = 2, 50, 200, 15, 5, 64
     a.scale = 0.125
-    a.impl = 4
+    a.impl = 5
     assert lib.vla_attention_bf16(ctypes.byref(a), None) == _lib.VLA_E_INVALID
     assert "impl" in _lib.last_error()
     a.impl = _lib.ATTN_TCGEN05_SHORT

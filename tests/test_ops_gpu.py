@@ -287,3 +287,62 @@ def test_attention_tcgen05_short(cuda, Lq, Lk, Hq, Hkv, causal, B, kv_len):
         ref[[i for i, n in enumerate(kv_len) if n == 0]] = 0.0
         ref = ref.reshape(B * Lq, -1)
     torch.testing.assert_close(o.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("Lq,Lk,Hq,Hkv,causal,B,kv_len", [
+    (113, 113, 15, 5, True, 3, None),        # C4 prefix: 3 x 113 stacked rows, causal
+    (128, 128, 15, 5, True, 1, None),        # C0 text: 384 stacked rows, 128 keys
+    (50, 50, 15, 5, True, 2, None),          # C3 expert self: 64-key variant
+    (50, 113, 15, 5, False, 3, [113, 60, 1]),  # C3 expert cross with key padding
+    (50, 128, 15, 5, False, 2, [0, 128]),      # a sequence with no keys writes zeros
+    (7, 33, 4, 2, False, 1, None),            # ragged: 14 stacked rows, 33 keys
+    (200, 97, 2, 2, True, 2, None),           # one head per kv head, 4 row tiles (2 smem stages)
+    (50, 50, 15, 5, True, 400, None),         # 2000 items: every CTA cycles its stages and TMEM slots
+])
+def test_attention_tcgen05_pipelined(cuda, Lq, Lk, Hq, Hkv, causal, B, kv_len):
+    """The pipelined short-sequence kernel (TMA in and out, warp-specialised, items
+    in flight) forced on, against the fp32 oracle."""
+    from vla_b200 import _lib, device as dev
+    q = _rand((B, Lq, Hq, 64), 41)
+    k = _rand((B, Lk, Hkv, 64), 42)
+    v = _rand((B, Lk, Hkv, 64), 43)
+    o = torch.full((B * Lq, Hq * 64), float("nan"), dtype=BF, device="cuda")
+    kl = None if kv_len is None else torch.tensor(kv_len, dtype=torch.int32, device="cuda")
+    dev.attention(q.reshape(B * Lq, -1).cuda(), k.reshape(B * Lk, -1).cuda(), v.reshape(B * Lk, -1).cuda(), o,
+                  batch=B, Lq=Lq, Lk=Lk, Hq=Hq, Hkv=Hkv, q_batch=Lq * Hq * 64, k_batch=Lk * Hkv * 64,
+                  v_batch=Lk * Hkv * 64, o_batch=Lq * Hq * 64, causal=causal, kv_len=kl,
+                  impl=_lib.ATTN_TCGEN05_PIPE)
+    dev.sync_check()
+    sel = slice(None) if B <= 8 else [0, 1, B // 2, B - 1]
+    ref = R.attention(q[sel], k[sel], v[sel], causal=causal, kv_len=kv_len, dt=torch.float32)
+    if kv_len is not None and 0 in kv_len:
+        ref[[i for i, n in enumerate(kv_len) if n == 0]] = 0.0
+    ours = o.view(B, Lq, -1)[sel].float().cpu()
+    torch.testing.assert_close(ours, ref.reshape(ours.shape), atol=2e-2, rtol=2e-2)
+
+
+def test_attention_tcgen05_pipelined_fused_qkv(cuda):
+    """Q/K/V as column views of the layer's fused [rows, Q | K | V] buffer (the
+    text / expert self-attention layout), output into a strided view; the result
+    matches the mma.sync kernel on the same problem."""
+    from vla_b200 import _lib, device as dev
+    B, L, Hq, Hkv = 37, 113, 15, 5
+    cols = (Hq + 2 * Hkv) * 64
+    qkv = _rand((B * L, cols), 44).cuda()
+    q, k, v = qkv[:, :Hq * 64], qkv[:, Hq * 64:(Hq + Hkv) * 64], qkv[:, (Hq + Hkv) * 64:]
+    outs = {}
+    for impl in (_lib.ATTN_TCGEN05_PIPE, _lib.ATTN_MMA_SYNC):
+        buf = torch.full((B * L, Hq * 64 + 64), float("nan"), dtype=BF, device="cuda")
+        o = buf[:, :Hq * 64]
+        dev.attention(q, k, v, o, batch=B, Lq=L, Lk=L, Hq=Hq, Hkv=Hkv, q_batch=L * cols, k_batch=L * cols,
+                      v_batch=L * cols, o_batch=L * (Hq * 64 + 64), causal=True, impl=impl)
+        dev.sync_check()
+        assert torch.isnan(buf[:, Hq * 64:]).all(), "the kernel wrote outside the output view"
+        outs[impl] = o.float().cpu()
+    torch.testing.assert_close(outs[_lib.ATTN_TCGEN05_PIPE], outs[_lib.ATTN_MMA_SYNC], atol=1e-2, rtol=1e-2)
+    x = qkv.view(B, L, cols).cpu()
+    for b in (0, B - 1):
+        ref = R.attention(x[b:b + 1, :, :Hq * 64].view(1, L, Hq, 64), x[b:b + 1, :, Hq * 64:(Hq + Hkv) * 64].view(
+            1, L, Hkv, 64), x[b:b + 1, :, (Hq + Hkv) * 64:].view(1, L, Hkv, 64), causal=True, dt=torch.float32)
+        torch.testing.assert_close(outs[_lib.ATTN_TCGEN05_PIPE][b * L:(b + 1) * L], ref.reshape(L, -1), atol=2e-2,
+                                   rtol=2e-2)

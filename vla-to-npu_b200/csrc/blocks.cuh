@@ -3,6 +3,7 @@
 // lives in a caller-provided workspace (no allocation here).
 #pragma once
 #include "attention.cuh"
+#include "attention_pipe.cuh"
 #include "attention_short.cuh"
 #include "attention_tc.cuh"
 #include "elementwise.cuh"
@@ -137,6 +138,83 @@ static int attention_short(const attn::Params& p, int batch, cudaStream_t st) {
   return launch_status("attn_short");
 }
 
+// 4-D bf16 tensor map of one attention operand viewed as (64 head elements,
+// heads, rows, sequences) with strides (128 B, row stride, sequence stride);
+// box = 64 x box_heads x box_rows x 1, 128-byte swizzle, zero fill outside.
+static int make_tmap_heads_4d(CUtensorMap* m, const void* ptr, int heads, int rows, int batch, long long row_stride,
+                              long long batch_stride, int box_heads, int box_rows) {
+  auto enc = tmap_encoder();
+  if (enc == nullptr) return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  // a single sequence may come with a zero sequence stride; any legal stride
+  // serves, the coordinate is always 0
+  const long long bstride = batch > 1 ? batch_stride : row_stride * rows;
+  cuuint64_t dims[4] = {64, (cuuint64_t)heads, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[3] = {128, (cuuint64_t)row_stride * 2, (cuuint64_t)bstride * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_heads, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled (4-D) failed (%d): heads=%d rows=%d batch=%d ld=%lld bs=%lld",
+                     (int)r, heads, rows, batch, row_stride, batch_stride);
+  return VLA_OK;
+}
+
+// Whether the pipelined short-sequence kernel takes this problem.
+static bool pipe_fits(const attn::Params& p, int batch) {
+  const int G = p.Hq / p.Hkv;
+  const long long rows = (long long)G * p.Lq;
+  return p.Lk >= 1 && p.Lk <= 128 && p.Lq <= 256 && G <= 256 && rows <= attn_pipe::kMaxTiles * attn_pipe::MT &&
+         (batch == 1 || (p.q_batch > 0 && p.k_batch > 0 && p.v_batch > 0 && p.o_batch > 0)) &&
+         (long long)batch * p.Hkv < (1ll << 31);
+}
+
+// pipelined short-sequence tcgen05 attention: one persistent warp-specialised
+// CTA per SM over (sequence, kv head) items, TMA in and out
+static int attention_pipe(const attn::Params& p, int batch, cudaStream_t st) {
+  VLA_CHECK_ARG(pipe_fits(p, batch), "attention (pipelined tcgen05): Lk=%d Lq=%d G*Lq=%lld outside the kernel's range",
+                p.Lk, p.Lq, (long long)(p.Hq / p.Hkv) * p.Lq);
+  const int G = p.Hq / p.Hkv;
+  const int NK = p.Lk <= 64 ? 64 : 128;
+  attn_pipe::Params pp{};
+  pp.Lq = p.Lq, pp.Lk = p.Lk, pp.G = G, pp.Hkv = p.Hkv, pp.batch = batch, pp.causal = p.causal;
+  pp.T = (G * p.Lq + attn_pipe::MT - 1) / attn_pipe::MT;
+  pp.q_tx = (uint32_t)(G * p.Lq * 128);
+  pp.stage_bytes = (uint32_t)(pp.T * attn_pipe::TILE_BYTES + 2 * NK * 128);
+  pp.kv_len = p.kv_len;
+  pp.scale_log2 = p.scale_log2;
+  const int smem_cap = device_info().max_smem_optin > 0 ? device_info().max_smem_optin : 232448;
+  const int avail = smem_cap - 2048;
+  pp.stages = avail / (int)pp.stage_bytes;
+  if (pp.stages > attn_pipe::kMaxStages) pp.stages = attn_pipe::kMaxStages;
+  VLA_CHECK_ARG(pp.stages >= 1, "attention (pipelined tcgen05): stage of %u bytes does not fit", pp.stage_bytes);
+  const int smem = 2048 + pp.stages * (int)pp.stage_bytes;
+  CUtensorMap tq, tk, tv, to;
+  int rc = make_tmap_heads_4d(&tq, p.q, p.Hq, p.Lq, batch, p.q_row, p.q_batch, G, p.Lq);
+  if (!rc) rc = make_tmap_heads_4d(&tk, p.k, p.Hkv, p.Lk, batch, p.k_row, p.k_batch, 1, NK);
+  if (!rc) rc = make_tmap_heads_4d(&tv, p.v, p.Hkv, p.Lk, batch, p.v_row, p.v_batch, 1, NK);
+  if (!rc) rc = make_tmap_heads_4d(&to, p.o, p.Hq, p.Lq, batch, p.o_row, p.o_batch, G, p.Lq);
+  if (rc) return rc;
+  auto kern = NK == 64 ? attn_pipe::attn_pipe_kernel<64> : attn_pipe::attn_pipe_kernel<128>;
+  static thread_local int attr_smem[2][32] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& cur = attr_smem[NK == 64][dev & 31];
+  if (cur < smem) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cur = smem;
+  }
+  const long long items = (long long)batch * p.Hkv;
+  const int sms = device_info().num_sms;
+  const int grid = (int)(items < sms ? items : sms);
+  prof_begin(st);
+  launch_k(kern, dim3(grid), dim3(attn_pipe::kThreads), smem, st, tq, tk, tv, to, pp);
+  prof_end(st, VLA_KIND_ATTENTION, 4.0 * batch * p.Hq * (double)p.Lq * p.Lk * 64,
+           2.0 * batch * ((double)p.Lq * p.Hq * 64 * 2 + (double)p.Lk * p.Hkv * 64 * 2));
+  return launch_status("attn_pipe");
+}
+
 static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl = VLA_ATTN_AUTO) {
   VLA_CHECK_ARG(p.q && p.k && p.v && p.o, "attention: null pointer");
   VLA_CHECK_ARG(batch >= 0 && p.Lq >= 0 && p.Lk >= 0 && p.Hq > 0 && p.Hkv > 0 && p.Hq % p.Hkv == 0,
@@ -157,6 +235,8 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl
   // either way, tcgen05 13 % faster; expert 3 x 50 rows: 59 % vs 78 %, mma.sync
   // 5-10 % faster)
   if (impl == VLA_ATTN_TCGEN05_SHORT) return attention_short(p, batch, st);
+  if (impl == VLA_ATTN_TCGEN05_PIPE)
+    return attention_pipe(p, batch, st);
   if (impl == VLA_ATTN_AUTO && p.Lk <= 128) {
     const long long g_rows = (long long)(p.Hq / p.Hkv) * p.Lq;
     const long long pad_short = ((g_rows + 127) / 128) * 128;

@@ -243,7 +243,7 @@ int vla_attention_bf16(const vla_attention_args* a, vla_stream_t stream) {
   p.causal = a->causal;
   p.kv_len = a->kv_len;
   p.scale_log2 = a->scale * 1.4426950408889634f;
-  VLA_CHECK_ARG(a->impl >= VLA_ATTN_AUTO && a->impl <= VLA_ATTN_TCGEN05_SHORT, "attention: unknown impl %d", a->impl);
+  VLA_CHECK_ARG(a->impl >= VLA_ATTN_AUTO && a->impl <= VLA_ATTN_TCGEN05_PIPE, "attention: unknown impl %d", a->impl);
   return blocks::attention(p, a->batch, as_stream(stream), a->impl);
 }
 

@@ -75,6 +75,7 @@ ATTN_AUTO = 0
 ATTN_MMA_SYNC = 1
 ATTN_TCGEN05 = 2
 ATTN_TCGEN05_SHORT = 3
+ATTN_TCGEN05_PIPE = 4
 
 
 class LlamaLayer(ctypes.Structure):
