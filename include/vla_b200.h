@@ -233,9 +233,11 @@ typedef struct vla_attention_args {
 } vla_attention_args;
 /* Attention kernels: AUTO picks the tcgen05 kernel (persistent, 128-row query
  * tiles, TMEM accumulators) for non-causal attention with Lk >= 256, the
- * short-sequence tcgen05 kernel (all keys of a sequence in one tile, the query
- * heads of a kv head stacked into 128-row tiles) for Lk <= 128, causal or not,
- * and the mma.sync kernel (64-row tiles) otherwise.  TCGEN05 supports
+ * pipelined short-sequence tcgen05 kernel (TCGEN05_PIPE below) for Lk <= 128,
+ * causal or not, when its shape limits hold, and the mma.sync kernel (64-row
+ * tiles) otherwise.  TCGEN05_SHORT (all keys of a sequence in one tile, the
+ * query heads of a kv head stacked into 128-row tiles, one item per CTA at a
+ * time) is selectable explicitly.  TCGEN05 supports
  * non-causal attention only and needs q_batch / k_batch / v_batch to be whole
  * multiples of the row strides; TCGEN05_SHORT needs Lk <= 128.
  * TCGEN05_PIPE is the pipelined short-sequence kernel (one warp-specialised
@@ -263,6 +265,21 @@ int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, i
  * and its 14,592-call host loop (vla/preprocessing_bf16.py:86-103). */
 int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, int32_t H, int32_t W, int32_t p,
                           vla_stream_t stream);
+
+/* Camera frames to model input: frames uint8 [B, H, W, 3] (row-major HWC, any
+ * H and W), bilinear resize to S x S with half-pixel centres and no
+ * antialiasing (torch F.interpolate(mode="bilinear", align_corners=False)),
+ * scaled to [-1, 1] as v * 2/255 - 1, bf16 out:
+ *   mode 0: out = image [B, 3, S, S] (NCHW, the input of vla_patch_im2col_bf16);
+ *   mode 1: out = the patch-embedding GEMM's A operand [B * (S/p)^2, 3 p p]
+ *           (column cin*p*p + ky*p + kx), i.e. resize + normalisation + im2col in
+ *           one pass; p a multiple of 8 dividing S.
+ * S must be a multiple of 8.  The reference feeds images that are already
+ * 512 x 512 floats (preprocessing_block, vla/preprocessing_bf16.py:105-109;
+ * vla/vla.py:318); this is the input side that turns camera frames into them,
+ * so hosts ship 1 byte per pixel channel instead of 2. */
+int vla_camera_preprocess_u8(const uint8_t* frames, int32_t B, int32_t H, int32_t W, int32_t S, int32_t p,
+                             int32_t mode, void* out, vla_stream_t stream);
 
 /* Token embedding gather: out[b*rows_per_seq + row_offset + t, :] =
  * table[ids[b*T + t], :] * scale (create_text_emb, vla/vla.py:169-174). */

@@ -3,6 +3,7 @@
 must not exceed the reference bf16 path's error (tests/parity.py)."""
 import pytest
 import torch
+import torch.nn.functional as F
 
 from oracle import smolvla_ref as R
 from parity import check
@@ -168,3 +169,63 @@ def test_launch_overlap_is_bit_exact(cuda):
         lib.vla_set_launch_overlap(1)
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
     assert torch.equal(outs[1][0], outs[1][1])
+
+
+def test_pipeline_camera_frames(cuda):
+    """uint8 camera frames [B, H, W, 3] through the model (resize + normalise + im2col
+    fused on the GPU) give exactly the actions of the equivalent bf16 images, eager
+    and through the streamed host API; frames of another size are resized."""
+    from vla_b200.model import SmolVLA
+    cfg = tiny_cfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, 3, seed=9)
+    S = cfg.vision.image
+    g = torch.Generator().manual_seed(9)
+    frames = torch.randint(0, 256, (3, S, S, 3), generator=g, dtype=torch.uint8)
+    images = (frames.permute(0, 3, 1, 2).float() * (2.0 / 255.0) - 1.0).to(BF)
+    rest = [obs[k].cuda() for k in ("token_ids", "state", "noise")]
+    m = SmolVLA(cfg, params, "cuda")
+    ref = m.infer(images.cuda(), *rest, use_graph=False).clone()
+    out = m.infer(frames.cuda(), *rest, use_graph=False).clone()
+    assert torch.equal(out, ref)
+    out_g = m.infer(frames.cuda(), *rest, use_graph=True).clone()
+    assert torch.equal(out_g, ref)
+    host = (frames.pin_memory(), obs["token_ids"].pin_memory(), obs["state"].pin_memory(), obs["noise"].pin_memory())
+    outs = [torch.empty(3, cfg.expert.chunk, cfg.expert.action_dim).pin_memory() for _ in range(2)]
+    m.infer_host_stream([host, host], outs)
+    assert torch.equal(outs[1], ref.cpu())
+    # a 96 x 160 camera: resized to S x S on the GPU, against the oracle on torch's resize
+    big = torch.randint(0, 256, (3, 96, 160, 3), generator=g, dtype=torch.uint8)
+    out_r = m.infer(big.cuda(), *rest, use_graph=False).clone()
+    resized = F.interpolate(big.permute(0, 3, 1, 2).float(), size=(S, S), mode="bilinear", align_corners=False,
+                            antialias=False) * (2.0 / 255.0) - 1.0
+    obs_r = dict(obs, images=resized)
+    ref32 = R.smolvla_chunk(obs_r, params, cfg, dt=F32)
+    refbf = R.smolvla_chunk(obs_r, params, cfg, dt=BF)
+    check(out_r, ref32, refbf, "pipeline tiny from resized camera frames")
+
+
+def test_infer_overlapped_matches_per_batch(cuda):
+    """Consecutive batches overlapped (batch k+1's vision / text half on one stream
+    while batch k's expert runs on another, alternating prefix K/V slots) give
+    exactly the per-batch results, for bf16 images and for uint8 camera frames."""
+    from vla_b200.model import SmolVLA
+    cfg = tiny_cfg()
+    params = W.smolvla_params(cfg, seed=0)
+    m = SmolVLA(cfg, params, "cuda")
+    for frames in (False, True):
+        batches, refs = [], []
+        for s in range(5):
+            obs = W.observation_batch(cfg, 2, seed=20 + s)
+            img = obs["images"]
+            if frames:
+                g = torch.Generator().manual_seed(30 + s)
+                img = torch.randint(0, 256, (2, 96, 112, 3), generator=g, dtype=torch.uint8)
+            host = (img.pin_memory(), obs["token_ids"].pin_memory(), obs["state"].pin_memory(),
+                    obs["noise"].pin_memory())
+            batches.append(host)
+            refs.append(m.infer(*(t.cuda() for t in host)).clone().cpu())
+        outs = [torch.empty(2, cfg.expert.chunk, cfg.expert.action_dim).pin_memory() for _ in range(5)]
+        m.infer_overlapped(batches, outs)
+        for o, r in zip(outs, refs):
+            assert torch.equal(o, r)

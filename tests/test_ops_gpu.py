@@ -346,3 +346,30 @@ def test_attention_tcgen05_pipelined_fused_qkv(cuda):
             1, L, Hkv, 64), x[b:b + 1, :, (Hq + Hkv) * 64:].view(1, L, Hkv, 64), causal=True, dt=torch.float32)
         torch.testing.assert_close(outs[_lib.ATTN_TCGEN05_PIPE][b * L:(b + 1) * L], ref.reshape(L, -1), atol=2e-2,
                                    rtol=2e-2)
+
+
+@pytest.mark.parametrize("B,H,W,S", [(2, 512, 512, 512), (3, 480, 640, 512), (1, 37, 50, 64), (2, 1024, 768, 128)])
+def test_camera_preprocess(cuda, B, H, W, S):
+    """uint8 HWC camera frames -> bilinear resize (half-pixel centres, no antialias)
+    -> [-1, 1] bf16, as the NCHW image and fused with im2col into the patch GEMM
+    operand, against torch's interpolate in fp32 on the same frames."""
+    from vla_b200 import device as dev
+    g = torch.Generator().manual_seed(51 + H)
+    frames = torch.randint(0, 256, (B, H, W, 3), generator=g, dtype=torch.uint8)
+    x = frames.permute(0, 3, 1, 2).float()
+    ref = F.interpolate(x, size=(S, S), mode="bilinear", align_corners=False, antialias=False) * (2.0 / 255.0) - 1.0
+    fd = frames.cuda()
+    img = torch.empty(B, 3, S, S, dtype=BF, device="cuda")
+    dev.camera_preprocess(fd, S, img)
+    dev.sync_check()
+    # one bf16 rounding of values in [-1, 1]: at most 2^-8 away
+    torch.testing.assert_close(img.float().cpu(), ref, atol=2.0 ** -8 + 1e-5, rtol=0)
+    if H == W == S:
+        assert torch.equal(img.float().cpu(), (x * (2.0 / 255.0) - 1.0).to(BF).float()), "identity resize is exact"
+    p = 16
+    patches = torch.empty(B * (S // p) ** 2, 3 * p * p, dtype=BF, device="cuda")
+    dev.camera_preprocess(fd, S, patches, patch=p)
+    ref_patches = torch.empty_like(patches)
+    dev.patch_im2col(img, p, ref_patches)
+    dev.sync_check()
+    assert torch.equal(patches, ref_patches), "fused im2col differs from resize + im2col"

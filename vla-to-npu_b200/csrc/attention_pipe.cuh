@@ -52,6 +52,7 @@ struct Params {
   int T;             // M-tiles per item
   int stages;        // smem stages
   uint32_t q_tx;     // bytes of one item's Q copy (R * 128)
+  uint32_t q_region; // R * 128 rounded up to 1024 (K and V tiles follow)
   uint32_t stage_bytes;
   const int* kv_len;
   float scale_log2;
@@ -94,7 +95,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars& bb = *reinterpret_cast<Bars*>(base);
   const uint32_t stage0 = smem_u32(base + 1024);
-  const uint32_t q_region = (uint32_t)p.T * TILE_BYTES;
+  // The Q copy fills R rows; the last M-tile's MMA also reads rows past R (up to
+  // T * 128), which lie in this stage's K / V tiles or padding: garbage query
+  // rows whose outputs are never stored.  stage_bytes >= T * 16 KB keeps those
+  // reads inside the stage.
+  const uint32_t q_region = p.q_region;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = p.batch * p.Hkv;
   const int my_items = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;

@@ -164,8 +164,8 @@ static int make_tmap_heads_4d(CUtensorMap* m, const void* ptr, int heads, int ro
 // Whether the pipelined short-sequence kernel takes this problem.
 static bool pipe_fits(const attn::Params& p, int batch) {
   const int G = p.Hq / p.Hkv;
-  const long long rows = (long long)G * p.Lq;
-  return p.Lk >= 1 && p.Lk <= 128 && p.Lq <= 256 && G <= 256 && rows <= attn_pipe::kMaxTiles * attn_pipe::MT &&
+  return p.Lk >= 1 && p.Lk <= 128 && p.Lq <= 256 && G <= 256 &&
+         (long long)G * p.Lq <= attn_pipe::kMaxTiles * attn_pipe::MT &&
          (batch == 1 || (p.q_batch > 0 && p.k_batch > 0 && p.v_batch > 0 && p.o_batch > 0)) &&
          (long long)batch * p.Hkv < (1ll << 31);
 }
@@ -173,15 +173,17 @@ static bool pipe_fits(const attn::Params& p, int batch) {
 // pipelined short-sequence tcgen05 attention: one persistent warp-specialised
 // CTA per SM over (sequence, kv head) items, TMA in and out
 static int attention_pipe(const attn::Params& p, int batch, cudaStream_t st) {
-  VLA_CHECK_ARG(pipe_fits(p, batch), "attention (pipelined tcgen05): Lk=%d Lq=%d G*Lq=%lld outside the kernel's range",
-                p.Lk, p.Lq, (long long)(p.Hq / p.Hkv) * p.Lq);
+  VLA_CHECK_ARG(pipe_fits(p, batch), "attention (pipelined tcgen05): Lk=%d Lq=%d G=%d outside the kernel's range",
+                p.Lk, p.Lq, p.Hq / p.Hkv);
   const int G = p.Hq / p.Hkv;
   const int NK = p.Lk <= 64 ? 64 : 128;
   attn_pipe::Params pp{};
   pp.Lq = p.Lq, pp.Lk = p.Lk, pp.G = G, pp.Hkv = p.Hkv, pp.batch = batch, pp.causal = p.causal;
   pp.T = (G * p.Lq + attn_pipe::MT - 1) / attn_pipe::MT;
   pp.q_tx = (uint32_t)(G * p.Lq * 128);
-  pp.stage_bytes = (uint32_t)(pp.T * attn_pipe::TILE_BYTES + 2 * NK * 128);
+  pp.q_region = (uint32_t)((G * p.Lq * 128 + 1023) / 1024 * 1024);
+  pp.stage_bytes = pp.q_region + 2u * NK * 128u;
+  if (pp.stage_bytes < (uint32_t)(pp.T * attn_pipe::TILE_BYTES)) pp.stage_bytes = (uint32_t)(pp.T * attn_pipe::TILE_BYTES);
   pp.kv_len = p.kv_len;
   pp.scale_log2 = p.scale_log2;
   const int smem_cap = device_info().max_smem_optin > 0 ? device_info().max_smem_optin : 232448;
@@ -235,7 +237,9 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl
   // either way, tcgen05 13 % faster; expert 3 x 50 rows: 59 % vs 78 %, mma.sync
   // 5-10 % faster)
   if (impl == VLA_ATTN_TCGEN05_SHORT) return attention_short(p, batch, st);
-  if (impl == VLA_ATTN_TCGEN05_PIPE)
+  // short sequences (text prefix, action expert): the pipelined kernel, 30-45 %
+  // faster than the one-chain-per-CTA kernels on all three shapes
+  if (impl == VLA_ATTN_TCGEN05_PIPE || (impl == VLA_ATTN_AUTO && pipe_fits(p, batch)))
     return attention_pipe(p, batch, st);
   if (impl == VLA_ATTN_AUTO && p.Lk <= 128) {
     const long long g_rows = (long long)(p.Hq / p.Hkv) * p.Lq;

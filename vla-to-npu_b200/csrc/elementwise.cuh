@@ -164,6 +164,59 @@ __global__ void im2col_kernel(const bf16* __restrict__ img, bf16* __restrict__ o
 // Token embedding gather with scale (create_text_emb, vla/vla.py:169-174):
 //   out[(b*rows_per_seq + row_offset + t), :] = table[ids[b*T + t], :] * scale
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Camera frames in: uint8 [B, H, W, 3] (HWC, the usual camera / video layout)
+// -> bilinear resize to S x S (half-pixel centres, no antialiasing: the rule of
+// torch.nn.functional.interpolate(mode="bilinear", align_corners=False)) ->
+// scaled to [-1, 1] as v * 2/255 - 1 -> bf16, written either as the NCHW image
+// [B, 3, S, S] (mode 0) or directly as the patch-embedding GEMM's A operand
+// [B * (S/p)^2, 3 p p] with column cin*p*p + ky*p + kx (mode 1: resize,
+// normalisation and im2col in one pass).  One thread makes 8 horizontally
+// adjacent output pixels of one channel (one 16-byte store).
+// ---------------------------------------------------------------------------
+template <typename I>
+__global__ void camera_preprocess_kernel(const uint8_t* __restrict__ img, bf16* __restrict__ out, int B, int H, int W,
+                                         int S, int p, int mode, float scale_y, float scale_x) {
+  pdl_prologue();
+  const int xv = S >> 3;
+  const I total = (I)B * 3 * S * xv;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+    const int x0 = (int)(i % xv) * 8;
+    const I r = i / xv;
+    const int y = (int)(r % S);
+    const int c = (int)((r / S) % 3);
+    const long long b = (long long)(r / ((I)S * 3));
+    float sy = ((float)y + 0.5f) * scale_y - 0.5f;
+    sy = sy < 0.f ? 0.f : sy;
+    const int y0 = (int)sy;
+    const int y1 = y0 + (y0 < H - 1 ? 1 : 0);
+    const float ly = sy - (float)y0, hy = 1.f - ly;
+    const uint8_t* row0 = img + ((b * H + y0) * (long long)W) * 3 + c;
+    const uint8_t* row1 = img + ((b * H + y1) * (long long)W) * 3 + c;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float sx = ((float)(x0 + j) + 0.5f) * scale_x - 0.5f;
+      sx = sx < 0.f ? 0.f : sx;
+      const int xa = (int)sx;
+      const int xb = xa + (xa < W - 1 ? 1 : 0);
+      const float lx = sx - (float)xa, hx = 1.f - lx;
+      const float top = hx * (float)__ldg(row0 + 3 * xa) + lx * (float)__ldg(row0 + 3 * xb);
+      const float bot = hx * (float)__ldg(row1 + 3 * xa) + lx * (float)__ldg(row1 + 3 * xb);
+      v[j] = __fadd_rn(__fmul_rn(hy * top + ly * bot, 2.f / 255.f), -1.f);  // x * 2/255 - 1, two roundings
+    }
+    bf16* dst;
+    if (mode == 0) {
+      dst = out + ((b * 3 + c) * S + y) * (long long)S + x0;
+    } else {
+      const int g = S / p;
+      const long long tok = (b * g + y / p) * g + x0 / p;
+      dst = out + tok * (3ll * p * p) + c * p * p + (y % p) * p + (x0 % p);
+    }
+    *reinterpret_cast<uint4*>(dst) = pack_bf16x8(v);
+  }
+}
+
 __global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict__ table, int vocab, int H, int B,
                              int T, float scale, bf16* __restrict__ out, long long ldo, int rows_per_seq,
                              int row_offset) {

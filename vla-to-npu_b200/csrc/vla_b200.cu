@@ -263,6 +263,23 @@ int vla_pixel_shuffle_bf16(const void* in, void* out, int32_t B, int32_t grid, i
   return launch_status("pixel_shuffle");
 }
 
+int vla_camera_preprocess_u8(const uint8_t* frames, int32_t B, int32_t H, int32_t W, int32_t S, int32_t p,
+                             int32_t mode, void* out, vla_stream_t stream) {
+  VLA_CHECK_ARG(frames && out && B >= 0 && H > 0 && W > 0 && S > 0 && S % 8 == 0 && (mode == 0 || mode == 1),
+                "camera_preprocess: bad arguments (S must be a positive multiple of 8, mode 0 or 1)");
+  VLA_CHECK_ARG(mode == 0 || (p > 0 && p % 8 == 0 && S % p == 0),
+                "camera_preprocess: patch mode needs p a multiple of 8 dividing S");
+  VLA_CHECK_ALIGN(aligned16(out), "camera_preprocess: output alignment");
+  if (B == 0) return VLA_OK;
+  const long long work = (long long)B * 3 * S * (S / 8);
+  prof_begin(as_stream(stream));
+  auto kern = work < (1ll << 30) ? ew::camera_preprocess_kernel<int> : ew::camera_preprocess_kernel<long long>;
+  launch_k(kern, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), frames, (bf16*)out, B, H, W, S,
+           p, mode, (float)H / (float)S, (float)W / (float)S);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, (double)B * H * W * 3 + 2.0 * B * 3 * S * S);
+  return launch_status("camera_preprocess");
+}
+
 int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, int32_t H, int32_t W, int32_t p,
                           vla_stream_t stream) {
   VLA_CHECK_ARG(img && out && B >= 0 && Cin > 0 && p > 0 && H % p == 0 && W % p == 0 && p % 8 == 0,

@@ -143,6 +143,7 @@ SIGNATURES = {
     "vla_patch_im2col_bf16": [_P, _P, _I32, _I32, _I32, _I32, _I32, _P],
     "vla_embed_bf16": [_P, _P, _I32, _I32, _I32, _I32, _F32, _P, _I64, _I32, _I32, _P],
     "vla_f32_to_bf16": [_P, _I64, _P, _I64, _I64, _I64, _P],
+    "vla_camera_preprocess_u8": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P],
     "vla_llama_layer_workspace": [ctypes.POINTER(LlamaLayer), _I64, _I32],
     "vla_llama_self_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, ctypes.c_size_t, _P],
     "vla_llama_cross_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, _I64, _I32, _P, _P,

@@ -145,6 +145,18 @@ def patch_im2col(img: torch.Tensor, patch: int, out: torch.Tensor) -> torch.Tens
     return out
 
 
+def camera_preprocess(frames: torch.Tensor, size: int, out: torch.Tensor, patch: int = 0) -> torch.Tensor:
+    """uint8 camera frames [B, H, W, 3] -> bf16 model input in [-1, 1], bilinearly
+    resized to size x size: the NCHW image [B, 3, size, size] when ``patch`` is 0,
+    else the patch-embedding GEMM operand [B * (size/patch)^2, 3 * patch^2]."""
+    if frames.dtype != torch.uint8 or frames.dim() != 4 or frames.shape[3] != 3 or not frames.is_contiguous():
+        raise ValueError("camera_preprocess: need contiguous uint8 frames [B, H, W, 3]")
+    B, H, W, _ = frames.shape
+    _lib.call("vla_camera_preprocess_u8", _ptr(frames), B, H, W, size, patch, 1 if patch else 0, _ptr(out),
+              _stream())
+    return out
+
+
 def embed(ids: torch.Tensor, table: torch.Tensor, scale: float, out: torch.Tensor, rows_per_seq: int,
           row_offset: int) -> torch.Tensor:
     B, T = ids.shape

@@ -152,6 +152,7 @@ class ActionExpert:
                 self.cross_index[i] = len(self.cross_index)
         self.batch = 0
         self.prefix_len = 0
+        self.slot = 0
         self.kv_len: Optional[torch.Tensor] = None
 
     def allocate(self, batch: int, prefix_len: int) -> None:
@@ -160,7 +161,11 @@ class ActionExpert:
         e, d = self.cfg.expert, self.device
         self.batch, self.prefix_len = batch, prefix_len
         rows_e = batch * e.chunk
-        self.kv_cross = torch.empty(len(self.cross_index), batch * prefix_len, 2 * e.kv_dim, dtype=BF16, device=d)
+        # two sets of projected prefix K/V: the next batch's text layers may fill
+        # one while the expert of the current batch reads the other
+        self.kv_slots = [torch.empty(len(self.cross_index), batch * prefix_len, 2 * e.kv_dim, dtype=BF16, device=d)
+                         for _ in range(2)]
+        self.noise_slots = [torch.empty(rows_e, e.action_dim, dtype=torch.float32, device=d) for _ in range(2)]
         self.x_t = torch.empty(rows_e, e.action_dim, dtype=torch.float32, device=d)
         self.x_b = torch.empty(rows_e, e.action_dim, dtype=BF16, device=d)
         self.h = torch.empty(rows_e, e.hidden, dtype=BF16, device=d)
@@ -169,6 +174,11 @@ class ActionExpert:
         lib = _lib.load()
         import ctypes
         self.ws.get(max(lib.vla_llama_layer_workspace(ctypes.byref(w.struct), rows_e, 1) for w in self.layers))
+
+    @property
+    def kv_cross(self) -> torch.Tensor:
+        """Projected prefix K/V [cross layers, B * prefix_len, 2 kv_dim] of the current slot."""
+        return self.kv_slots[self.slot]
 
     def project_prefix_kv(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
         """Cross layer ``layer``'s K/V from the prefix K/V [B * prefix_len, text kv_dim]."""
@@ -248,11 +258,17 @@ class SmolVLA:
         self.text = [LlamaLayerWeights(p, t, d) for p in params["text"]]
         self.rope_text = rope_table(pf.length, t.head_dim, t.rope_theta).to(d)
         self.ws = dev.Workspace(d)
-        self.action = ActionExpert(cfg, params, d, self.ws)
+        # the expert has its own scratch, so that its kernels and the next batch's
+        # vision / text kernels can run at the same time (infer_overlapped)
+        self.action = ActionExpert(cfg, params, d)
         self.expert = self.action.layers
         self.batch = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.graph_batch = 0
+        self.ov_graphs = None
+        self.ov_batch = 0
+        self.frames_input = False
+        self.in_frames: Optional[torch.Tensor] = None
 
     # -- buffers ----------------------------------------------------------
     def allocate(self, batch: int) -> None:
@@ -263,6 +279,8 @@ class SmolVLA:
         self.batch = batch
         B = batch
         self.in_images = torch.empty(B, v.channels, v.image, v.image, dtype=BF16, device=d)
+        self.in_frames = None  # uint8 camera frames [B, H, W, 3], allocated when frames are given
+        self.frames_input = False
         self.in_ids = torch.empty(B, pf.text_tokens, dtype=torch.int32, device=d)
         self.in_state = torch.empty(B, pf.state_dim, dtype=BF16, device=d)
         self.in_noise = torch.empty(B * e.chunk, e.action_dim, dtype=torch.float32, device=d)
@@ -284,14 +302,18 @@ class SmolVLA:
             lib.vla_llama_layer_workspace(ctypes.byref(self.text[0].struct), rows_t, 0),
         )
         self.ws.get(need)
-        self.graph = None
+        self._invalidate()
 
     # -- stages -----------------------------------------------------------
     def vision_tower(self) -> None:
         cfg = self.cfg
         v, t, pf = cfg.vision, cfg.text, cfg.prefix
         B = self.batch
-        dev.patch_im2col(self.in_images, v.patch, self.patches)
+        if self.frames_input:
+            # camera frames: resize + normalisation + im2col in one kernel
+            dev.camera_preprocess(self.in_frames, v.image, self.patches, patch=v.patch)
+        else:
+            dev.patch_im2col(self.in_images, v.patch, self.patches)
         dev.gemm(self.patches, self.w_patch, self.x_vis,
                  dev.make_epilogue(bias=self.b_patch, residual=self.pos_emb, res_row_mod=v.tokens))
         for lw in self.vision:
@@ -324,6 +346,20 @@ class SmolVLA:
         self.x_t.copy_(self.in_noise)
         self.action.run()
 
+    # -- the two halves of a chunk, for overlapping consecutive batches --------
+    def forward_front(self) -> None:
+        """Vision tower, prefix, text layers and the expert's prefix K/V projections
+        into K/V slot ``self.action.slot``; the batch's noise is parked in the same slot."""
+        self.vision_tower()
+        self.prefix_tokens()
+        self.text_layers()
+        self.action.noise_slots[self.action.slot].copy_(self.in_noise)
+
+    def forward_back(self) -> None:
+        """The expert's 10 Euler steps on K/V slot ``self.action.slot``."""
+        self.x_t.copy_(self.action.noise_slots[self.action.slot])
+        self.action.run()
+
     def forward_device(self) -> torch.Tensor:
         """Launch the whole chunk forward on the current stream from the input buffers."""
         self.vision_tower()
@@ -343,6 +379,10 @@ class SmolVLA:
         self.graph = g
         self.graph_batch = self.batch
 
+    def _invalidate(self) -> None:
+        self.graph = None
+        self.ov_graphs = None
+
     def replay(self) -> torch.Tensor:
         if self.graph is None or self.graph_batch != self.batch:
             self.capture()
@@ -354,10 +394,31 @@ class SmolVLA:
         """Copy one batch of observations (host or device tensors) into the input buffers."""
         B = images.shape[0]
         self.allocate(B)
-        self.in_images.copy_(images.to(BF16) if images.dtype != BF16 else images, non_blocking=non_blocking)
+        self._image_buffer(images).copy_(images.to(BF16) if images.dtype not in (BF16, torch.uint8) else images,
+                                         non_blocking=non_blocking)
         self.in_ids.copy_(token_ids, non_blocking=non_blocking)
         self.in_state.copy_(state.to(BF16) if state.dtype != BF16 else state, non_blocking=non_blocking)
         self.in_noise.copy_(noise.reshape(B * self.cfg.expert.chunk, -1), non_blocking=non_blocking)
+
+    def _image_buffer(self, images: torch.Tensor) -> torch.Tensor:
+        """The device buffer an image batch is copied into: uint8 camera frames
+        [B, H, W, 3] (any H, W; resized on the GPU) or images [B, 3, S, S] already
+        scaled to [-1, 1].  Switching between the two re-captures the graph."""
+        frames = images.dtype == torch.uint8
+        if frames:
+            if images.dim() != 4 or images.shape[3] != 3:
+                raise ValueError("uint8 camera frames must be [B, H, W, 3]")
+            if self.in_frames is None or self.in_frames.shape != images.shape:
+                self.in_frames = torch.empty(images.shape, dtype=torch.uint8, device=self.device)
+                self._invalidate()
+        if frames != self.frames_input:
+            self.frames_input = frames
+            self._invalidate()
+        return self.in_frames if frames else self.in_images
+
+    def _inputs(self):
+        img = self.in_frames if self.frames_input else self.in_images
+        return (img, self.in_ids, self.in_state, self.in_noise)
 
     def infer_host(self, images, token_ids, state, noise, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """End-to-end call from host memory: copy the observations in (pinned host
@@ -378,19 +439,21 @@ class SmolVLA:
         stream (into one of two device staging sets) while batch k computes, and
         each batch's actions are copied device->host into ``outs[k]`` (pinned)
         right after its chunk graph.  ``batches`` holds (images, token_ids, state,
-        noise) tuples of pinned host tensors of one batch size.  Returns ``outs``
+        noise) tuples of pinned host tensors of one batch size; images are either
+        uint8 camera frames [B, H, W, 3] or bf16 images [B, 3, S, S] in [-1, 1].  Returns ``outs``
         after the last copy completed."""
         n = len(batches)
         if n == 0:
             return outs
         B = batches[0][0].shape[0]
         self.allocate(B)
+        self._image_buffer(batches[0][0])
         if self.graph is None or self.graph_batch != B:
             self.capture()
-        if getattr(self, "_stage_batch", 0) != B:
-            self._stage = [[torch.empty_like(t) for t in (self.in_images, self.in_ids, self.in_state, self.in_noise)]
-                           for _ in range(2)]
-            self._stage_batch = B
+        key = (B, tuple(batches[0][0].shape), batches[0][0].dtype)
+        if getattr(self, "_stage_key", None) != key:
+            self._stage = [[torch.empty_like(t) for t in self._inputs()] for _ in range(2)]
+            self._stage_key = key
             self._copy_stream = torch.cuda.Stream(self.device)
         comp = torch.cuda.current_stream(self.device)
         cs = self._copy_stream
@@ -415,12 +478,100 @@ class SmolVLA:
                 h2d(k + 1)
             st = self._stage[k & 1]
             comp.wait_event(copied[k & 1])
-            for dst, src in zip((self.in_images, self.in_ids, self.in_state, self.in_noise), st):
+            for dst, src in zip(self._inputs(), st):
                 dst.copy_(src, non_blocking=True)
             consumed[k & 1].record(comp)
             self.graph.replay()
             outs[k].view(-1, self.cfg.expert.action_dim).copy_(self.x_t, non_blocking=True)
         comp.synchronize()
+        return outs
+
+    def _capture_halves(self) -> None:
+        """CUDA graphs of the two chunk halves for both K/V slots."""
+        graphs = []
+        for slot in (0, 1):
+            self.action.slot = slot
+            self.forward_front()  # warm-up
+            self.forward_back()
+            torch.cuda.synchronize(self.device)
+            gf, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gf):
+                self.forward_front()
+            with torch.cuda.graph(gb):
+                self.forward_back()
+            graphs.append((gf, gb))
+        self.action.slot = 0
+        torch.cuda.synchronize(self.device)
+        self.ov_graphs = graphs
+        self.ov_batch = self.batch
+
+    def infer_overlapped(self, batches, outs) -> list:
+        """Streamed inference that overlaps consecutive batches: batch k+1's vision
+        tower, prefix and text layers (front half) run on one stream while batch
+        k's 10-step action expert (back half) runs on another, on alternating
+        slots of the expert's prefix K/V; host->device copies of batch k+2 run on a
+        third.  Same inputs and outputs as infer_host_stream (pinned host
+        batches, ``outs[k]`` receives batch k's actions) and the same results."""
+        n = len(batches)
+        if n == 0:
+            return outs
+        B = batches[0][0].shape[0]
+        self.allocate(B)
+        self._image_buffer(batches[0][0])
+        if getattr(self, "ov_graphs", None) is None or self.ov_batch != B:
+            self._capture_halves()
+        key = (B, tuple(batches[0][0].shape), batches[0][0].dtype)
+        if getattr(self, "_stage_key", None) != key:
+            self._stage = [[torch.empty_like(t) for t in self._inputs()] for _ in range(2)]
+            self._stage_key = key
+            self._copy_stream = torch.cuda.Stream(self.device)
+        if getattr(self, "_ov_streams", None) is None:
+            self._ov_streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+        sf, sb = self._ov_streams
+        cs = self._copy_stream
+        main = torch.cuda.current_stream(self.device)
+        sf.wait_stream(main)
+        sb.wait_stream(main)
+        cs.wait_stream(main)
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        copied, consumed, front_done, back_done = ([ev(), ev()] for _ in range(4))
+
+        def h2d(k):
+            st = self._stage[k & 1]
+            with torch.cuda.stream(cs):
+                if k >= 2:
+                    cs.wait_event(consumed[k & 1])
+                imgs, ids, state, noise = batches[k]
+                st[0].copy_(imgs, non_blocking=True)
+                st[1].copy_(ids, non_blocking=True)
+                st[2].copy_(state, non_blocking=True)
+                st[3].copy_(noise.reshape(st[3].shape), non_blocking=True)
+                copied[k & 1].record(cs)
+
+        h2d(0)
+        if n > 1:
+            h2d(1)
+        for k in range(n):
+            slot = k & 1
+            with torch.cuda.stream(sf):
+                sf.wait_event(copied[slot])
+                for dst, src in zip(self._inputs(), self._stage[slot]):
+                    dst.copy_(src, non_blocking=True)
+                consumed[slot].record(sf)
+                if k >= 2:
+                    sf.wait_event(back_done[slot])  # the expert of batch k-2 has read this K/V slot
+                self.ov_graphs[slot][0].replay()
+                front_done[slot].record(sf)
+            if k + 2 < n:
+                h2d(k + 2)
+            with torch.cuda.stream(sb):
+                sb.wait_event(front_done[slot])
+                self.ov_graphs[slot][1].replay()
+                outs[k].view(-1, self.cfg.expert.action_dim).copy_(self.x_t, non_blocking=True)
+                back_done[slot].record(sb)
+        main.wait_stream(sb)
+        main.wait_stream(sf)
+        main.synchronize()
         return outs
 
     def infer(self, images, token_ids, state, noise, use_graph: bool = True) -> torch.Tensor:
