@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--ctas", type=int, default=0, choices=[0, 1, 2],
                     help="GEMM kernel cases: force one CTA (1) or a CTA pair (2) per tile; 0 = automatic")
     ap.add_argument("--tile-n", type=int, default=0, help="GEMM kernel cases: force the tile width BN; 0 = automatic")
+    ap.add_argument("--splits", type=int, default=None,
+                    help="GEMM kernel cases: one-CTA tiles with the K split over this many CTAs (1 = none, 0 = auto)")
     ap.add_argument("--attn-impl", type=int, default=0,
                     help="attention kernel cases: VLA_ATTN_* kernel choice (0 = automatic)")
     return ap.parse_args()
@@ -84,6 +86,10 @@ KERNEL_CASES = {
     "attn_exp_self": "action-expert causal self-attention, 512 x 15 q / 5 kv heads x 50 x 50 (AUTO kernel choice)",
     "attn_exp_cross": "action-expert cross-attention to the prefix, 512 x 15 q / 5 kv heads x 50 x 113 (AUTO)",
     "gemm_fc1_full": "SigLIP fc1 GEMM + bias + GELU at the bench step's shape, M=262144 N=3072 K=768 (2 GB)",
+    "gemm_b1_down": "one observation's action-expert down projection + residual, M=50 N=720 K=2048",
+    "gemm_b1_o": "one observation's action-expert output projection + residual, M=50 N=720 K=960",
+    "gemm_b1_qkv": "one observation's action-expert QKV + RoPE, M=50 N=1600 K=720",
+    "gemm_b1_gu": "one observation's action-expert gate/up + SwiGLU, M=50 N=4096 K=720",
 }
 
 
@@ -101,22 +107,28 @@ def run_kernel_case(args):
                    "gemm_fc2": (16384, 768, 3072), "gemm_plain": (16384, 3072, 768),
                    "gemm_plain_k3072": (16384, 3072, 3072), "gemm_exp_down": (12800, 720, 2048),
                    "gemm_exp_o": (12800, 720, 960), "gemm_exp_qkv": (12800, 1600, 720),
-                   "gemm_exp_gu": (12800, 4096, 720)}[name]
+                   "gemm_exp_gu": (12800, 4096, 720), "gemm_b1_down": (50, 720, 2048), "gemm_b1_o": (50, 720, 960),
+                   "gemm_b1_qkv": (50, 1600, 720), "gemm_b1_gu": (50, 4096, 720)}[name]
         a = W.randn((M, K), 0, "kc.a").cuda()
         w = W.randn((N, K), 0, "kc.w", std=0.02).cuda()
         b = W.randn((N,), 0, "kc.b", std=0.01).cuda()
-        c = torch.empty(M, N // 2 if name == "gemm_exp_gu" else N, dtype=bf, device="cuda")
-        res = W.randn((M, N), 0, "kc.r").cuda() if name in ("gemm_fc2", "gemm_exp_down", "gemm_exp_o") else None
-        plain = name.startswith("gemm_plain") or name.startswith("gemm_exp")
+        swiglu = name in ("gemm_exp_gu", "gemm_b1_gu")
+        c = torch.empty(M, N // 2 if swiglu else N, dtype=bf, device="cuda")
+        res = (W.randn((M, N), 0, "kc.r").cuda()
+               if name in ("gemm_fc2", "gemm_exp_down", "gemm_exp_o", "gemm_b1_down", "gemm_b1_o") else None)
+        plain = name.startswith("gemm_plain") or name.startswith("gemm_exp") or name.startswith("gemm_b1")
         epi = dev.make_epilogue(bias=None if plain else b, residual=res,
                                 act=_lib.ACT_GELU_TANH if name.startswith("gemm_fc1") else 0)
-        if name == "gemm_exp_qkv":
+        if name in ("gemm_exp_qkv", "gemm_b1_qkv"):
             from vla_b200.model import rope_table
             cs = rope_table(50, 64, 10_000.0).cuda()
             epi = dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=1280)
-        elif name == "gemm_exp_gu":
+        elif swiglu:
             epi = dev.make_epilogue(act=_lib.ACT_SWIGLU)
-        fn = lambda: dev.gemm(a, w, c, epi, tile_n=args.tile_n, ctas=args.ctas)  # noqa: E731
+        if args.splits is not None:
+            fn = lambda: dev.gemm(a, w, c, epi, tile_n=args.tile_n, splits=args.splits)  # noqa: E731
+        else:
+            fn = lambda: dev.gemm(a, w, c, epi, tile_n=args.tile_n, ctas=args.ctas)  # noqa: E731
         out_cols = c.shape[1]
         flops, nbytes = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * out_cols * (2 if res is not None else 1))
     elif name == "attn_vision":
@@ -171,10 +183,17 @@ def run_kernel_case(args):
     for _ in range(max(args.warmup, 1)):
         fn()
     torch.cuda.synchronize()
+    # the timed launches replay as one CUDA graph, so that host launch cost (ctypes,
+    # tensor-map encoding) does not set the pace of short kernels
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        fn()
+    graph.replay()
     e1.record()
     e1.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
@@ -440,7 +459,7 @@ def profile_pass(model) -> dict:
 #       -k regex:gemm -s 3 -c 1 python bench.py --kernel-case gemm_fc1_full --steps 2 --warmup 3
 # (M N K) -> bytes.  Algorithmic minimum for the fc1 shape: A 402.7 MB + W 4.7 MB +
 # C 1610.6 MB = 2018 MB.
-DRAM_TRAFFIC_PER_LAUNCH = {}
+DRAM_TRAFFIC_PER_LAUNCH = {(262144, 3072, 768): 408.94e6 + 1.56e9}
 
 
 # Algorithmic work of the benchmark blocks at B = 1 (valid tokens only; attention

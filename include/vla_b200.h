@@ -167,6 +167,20 @@ int vla_gemm_bf16_tiled(const void* A, int64_t lda, const void* B, int64_t ldb, 
 int vla_gemm_bf16_ex(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
                      int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, int32_t ctas, vla_stream_t stream);
 
+/* The GEMM on one-CTA tiles with the K extent split over a cluster of
+ * `splits` CTAs (2..8) per output tile: each CTA multiplies its contiguous
+ * share of the k-blocks, the partial fp32 tiles are summed in the leading
+ * CTA's shared memory (distributed shared memory, no global scratch) and the
+ * leader runs the fused epilogue.  It puts more SMs on the weight stream of
+ * outputs with few tiles, but at one observation (M = 50) the clustered launch
+ * measured slower than the plain one, so vla_gemm_bf16 never splits by itself.
+ * splits 2..8 (at most 5 CTAs at tile_n 64, 2 at 128; at most one CTA per
+ * k-block), 1 = no split, 0 = the launcher's choice (no split); tile_n 0 / 32
+ * / 64 / 128. */
+int vla_gemm_bf16_split(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                        int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, int32_t splits,
+                        vla_stream_t stream);
+
 /* Row normalisation over bf16 rows of width N (N % 8 == 0), fp32 statistics.
  * RMSNorm:  y = x * rsqrt(mean(x^2) + eps) * g
  *   replaces rms_norm_960_bf16 (cc/bf16/rms_norm_960_bf16.cc:60-62) and
@@ -280,6 +294,13 @@ int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, in
  * so hosts ship 1 byte per pixel channel instead of 2. */
 int vla_camera_preprocess_u8(const uint8_t* frames, int32_t B, int32_t H, int32_t W, int32_t S, int32_t p,
                              int32_t mode, void* out, vla_stream_t stream);
+
+/* Camera of the closed-loop PushT demo (the reference renders it with
+ * matplotlib, simulation/pusht_env.py:196-264): scene fp32 [n, 8] = end effector
+ * x, y; block x, y, theta; target x, y, theta (512 x 512 workspace, y up) ->
+ * frames uint8 [n, S, S, 3]: background, target T outline, block T, end
+ * effector disc. */
+int vla_pusht_render_u8(const float* scene, int32_t n, int32_t S, uint8_t* frames, vla_stream_t stream);
 
 /* Token embedding gather: out[b*rows_per_seq + row_offset + t, :] =
  * table[ids[b*T + t], :] * scale (create_text_emb, vla/vla.py:169-174). */

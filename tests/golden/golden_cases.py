@@ -37,6 +37,9 @@ CASES = {
     "siglip_emb": dict(kind="siglip_emb", consts=dict(EMBED=128, IMAGE=64, PATCH=16)),
     "con_ref": dict(kind="con_ref", consts={}),
     "masked_softmax_cpu": dict(kind="masked_softmax_cpu", consts=dict(SEQ=32)),
+    # simulation/pusht_env.py module constants
+    "pusht": dict(kind="pusht", consts=dict(WORKSPACE=512, EE_RADIUS=15, BLOCK_W=80, BLOCK_H=30, PUSH_COEFF=0.15,
+                                            FRICTION=0.7)),
 }
 
 SEED = 1234
@@ -84,6 +87,8 @@ def case_inputs(name: str) -> dict:
         x = W.randn((1024, 768), SEED, "golden.con.x")
         w = W.randn((12288, 960), SEED, "golden.con.W", std=0.02)
         return {"params": {"W": w}, "x": x}
+    if kind == "pusht":
+        return {"params": {}, "seeds": [0, 3, 99], "steps": 150}
     if kind == "masked_softmax_cpu":
         x = W.randn((32, 32), SEED, "golden.msm.x", std=2.0)
         return {"params": {}, "x": x}

@@ -15,6 +15,9 @@ supplies their module-level constants:
   MiniVit                   vla/vision_block_bf16.py:57-79
   SiglipVisionConfig/Embeddings  vla/vit_emb.py:19-47
   con_ref                   vla/vla.py:434-437
+  PushTEnv (+ make_t_shape, point_in_polygon, circle_polygon_overlap)
+                            simulation/pusht_env.py:29-194 (physics only;
+                            its matplotlib rendering is not executed)
 
 torchtune.modules.MultiHeadAttention is used by TextEncoderBlock only as a
 holder of its q/k/v/output projections (the forward never calls it), so a
@@ -139,6 +142,22 @@ def run(ref_root: str) -> dict:
             x = inp["x"].float().numpy()
             y = ns["con_ref"](x, {"W": p["W"].float().numpy()})
             out[name] = np.asarray(y, dtype=np.float32)
+            continue
+        elif kind == "pusht":
+            ns = load_defs(os.path.join(ref_root, "simulation/pusht_env.py"),
+                           ["make_t_shape", "point_in_polygon", "circle_polygon_overlap", "PushTEnv"], c)
+            for seed in inp["seeds"]:
+                env = ns["PushTEnv"](seed=seed)
+                states, actions = [env.get_state()], []
+                rng = np.random.default_rng(1000 + seed)
+                for t in range(inp["steps"]):
+                    # head for the block, then push through it, with noise: plenty of contacts
+                    to_b = np.array([env.block_x - env.ee_x, env.block_y - env.ee_y])
+                    a = to_b / max(np.linalg.norm(to_b), 1e-6) * 6.0 + rng.normal(0, 0.5, 2)
+                    actions.append(a)
+                    states.append(env.step(a))
+                out[f"{name}.{seed}.actions"] = np.array(actions, dtype=np.float64)
+                out[f"{name}.{seed}.states"] = np.array(states, dtype=np.float32)
             continue
         elif kind == "masked_softmax_cpu":
             ns = load_defs(os.path.join(ref_root, "vla/action_expert_bf16.py"), ["masked_softmax_cpu"], c)

@@ -141,3 +141,88 @@ def test_gemm_rope_tile_widths(cuda, tile_n, ctas):
     ref = torch.cat([rot, y[:, nrot:]], 1) + r.float()
     torch.testing.assert_close(out.float().cpu(), ref, atol=4e-2, rtol=2e-2)
     dev.sync_check()
+
+
+@pytest.mark.parametrize("splits", [2, 3, 4, 8])
+@pytest.mark.parametrize("tile_n", [32, 64, 128])
+@pytest.mark.parametrize("M,N,K", [(50, 720, 2048), (113, 960, 2560), (7, 1600, 720), (300, 256, 960)])
+def test_gemm_split_k(cuda, splits, tile_n, M, N, K):
+    """K split over a cluster of CTAs, partial tiles summed through distributed
+    shared memory: plain product (300 rows: several tiles per cluster in turn).
+    Wider tiles leave room for fewer partial slots (64: 5 CTAs, 128: 2); larger
+    splits are rejected."""
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    if splits > {32: 8, 64: 5, 128: 2}[tile_n]:
+        a = torch.zeros(M, K, dtype=torch.bfloat16, device="cuda")
+        w = torch.zeros(N, K, dtype=torch.bfloat16, device="cuda")
+        with pytest.raises(_lib.VlaError):
+            dev.gemm(a, w, torch.empty(M, N, dtype=torch.bfloat16, device="cuda"), tile_n=tile_n, splits=splits)
+        return
+    g = torch.Generator().manual_seed(M + N + K + splits)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dev.gemm(a, w, out, tile_n=tile_n, splits=splits)
+    dev.sync_check()
+    torch.testing.assert_close(out.float(), _ref(a, w), atol=3e-2, rtol=1e-2)
+
+
+def test_gemm_split_k_epilogues(cuda):
+    """Every fused epilogue behind the split-K reduction matches the same GEMM
+    without the split (fp32 sums in another order: within a bf16 rounding)."""
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    from vla_b200.model import interleave_gate_up, rope_table
+    g = torch.Generator().manual_seed(77)
+    M, K = 50, 720
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
+    cases = []
+    w = (torch.randn(720, K, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    res = torch.randn(M, 720, generator=g).to(torch.bfloat16).cuda()
+    bias = (torch.randn(720, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    cases.append(("bias+gelu+residual", w, 720, lambda: dev.make_epilogue(bias=bias, act=_lib.ACT_GELU_TANH,
+                                                                          residual=res)))
+    wg, wu = (torch.randn(K, 2048, generator=g) * 0.05), (torch.randn(K, 2048, generator=g) * 0.05)
+    wgu = interleave_gate_up(wg, wu, "cuda")
+    cases.append(("swiglu", wgu, 2048, lambda: dev.make_epilogue(act=_lib.ACT_SWIGLU)))
+    wq = (torch.randn(1600, K, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    cs = rope_table(50, 64, 1e4).cuda()
+    cases.append(("rope", wq, 1600, lambda: dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50,
+                                                               rope_ncols=1280)))
+    wo = (torch.randn(32, K, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    x0 = torch.randn(M, 32, generator=g).cuda()
+    for name, wt, ncols, mk in cases:
+        outs = []
+        for splits in (1, 4):
+            out = torch.full((M, ncols), float("nan"), dtype=torch.bfloat16, device="cuda")
+            dev.gemm(a, wt, out, mk(), tile_n=32 if name != "rope" else 64, splits=splits)
+            dev.sync_check()
+            outs.append(out.float())
+        torch.testing.assert_close(outs[1], outs[0], atol=2e-2, rtol=1e-2, msg=name)
+    # Euler: x += dt * (a @ wo^T) in fp32, C = bf16(x)
+    xs, cb = [], []
+    for splits in (1, 4):
+        x = x0.clone()
+        c = torch.empty(M, 32, dtype=torch.bfloat16, device="cuda")
+        dev.gemm(a, wo, c, dev.make_epilogue(act=_lib.ACT_EULER, euler_x=x, euler_dt=-0.1), tile_n=32, splits=splits)
+        dev.sync_check()
+        xs.append(x)
+        cb.append(c.float())
+    torch.testing.assert_close(xs[1], xs[0], atol=1e-3, rtol=1e-3)
+    ref = x0 - 0.1 * (a.float() @ wo.float().T)
+    torch.testing.assert_close(xs[1], ref, atol=2e-3, rtol=1e-3)
+
+
+def test_gemm_split_k_rejects_bad_requests(cuda):
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    a = torch.zeros(50, 128, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(64, 128, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(50, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.VlaError):
+        dev.gemm(a, w, out, tile_n=32, splits=9)
+    with pytest.raises(_lib.VlaError):
+        dev.gemm(a, w, out, tile_n=32, splits=4)  # 2 k-blocks cannot feed 4 CTAs
+    with pytest.raises(_lib.VlaError):
+        dev.gemm(a, w, out, tile_n=96, splits=2)

@@ -127,3 +127,21 @@ def test_cross_attention_block():
     x, ctx = inp["args"]
     out = R.cross_attention_block(x, ctx, inp["params"], LLAMA_CFG, dt=BF)
     _cmp(out, "cross_attn.bf16")
+
+
+@pytest.mark.parametrize("seed", [0, 3, 99])
+def test_pusht_physics_matches_reference_env(seed):
+    """vla_b200.pusht.PushTBatch restates simulation/pusht_env.py's physics; on the
+    reference environment's own trajectories (reset from the seed, 150 steps of
+    pushes with contact) it reproduces every state, and batching environments
+    changes nothing."""
+    from vla_b200.pusht import PushTBatch
+    acts = GOLD[f"pusht.{seed}.actions"]
+    ref = GOLD[f"pusht.{seed}.states"]
+    env = PushTBatch(1, seed)
+    got = [env.state()[0]] + [env.step(a[None])[0] for a in acts]
+    np.testing.assert_allclose(np.array(got), ref, atol=1e-6, rtol=0)
+    # three environments at once, this seed in the middle
+    envs = PushTBatch(3, [seed + 7, seed, seed + 11])
+    got3 = [envs.state()[1]] + [envs.step(np.stack([a * 0.5, a, -a]))[1] for a in acts]
+    np.testing.assert_allclose(np.array(got3), ref, atol=1e-6, rtol=0)

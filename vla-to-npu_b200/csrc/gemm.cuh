@@ -291,6 +291,13 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
     if (i < nv) cp[i] = pack_bf16x8(v + 8 * i);
 }
 
+// Partial accumulators of other CTAs added to this CTA's TMEM values right after
+// each TMEM load (split-K, gemm_splitk.cuh); the plain kernels use NoPartial,
+// which compiles to nothing.
+struct NoPartial {
+  __device__ __forceinline__ void add16(int, float*) const {}
+};
+
 // RoPE epilogue of row m over the 64-wide heads of a BN-wide tile: rotate pairs
 // (d, d+32), d < 32.  The pairs split into two halves (d < 16, d >= 16); with an
 // even number of warps per lane quarter each warp owns one half of every head it
@@ -298,10 +305,10 @@ __device__ __forceinline__ void finish32(const DevEpi& ep, int m, int n, long lo
 // tile and reuses them for all heads (every thread reads its own table row, so
 // each table load touches 32 cache lines: reloading it per head made the RoPE
 // GEMMs bound by L1 wavefronts).
-template <int BN>
+template <int BN, class PS = NoPartial>
 __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, long long orow,
                                           bool row_ok, int part, int nparts, const CUtensorMap* tmC, EpiStore& es,
-                                          int lane) {
+                                          int lane, const PS& ps = PS()) {
   const bool split = (nparts & 1) == 0;
   const int hq0 = split ? (part & 1) : 0;
   const int hq1 = split ? (part & 1) : 1;
@@ -318,6 +325,8 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
       if (n >= ep.N) break;
       float lo[16], hi[16];
       tmem_ld16x2(taddr + 64 * h + 16 * hq, taddr + 64 * h + 32 + 16 * hq, lo, hi);
+      ps.add16(64 * h + 16 * hq, lo);
+      ps.add16(64 * h + 32 + 16 * hq, hi);
       if (!row_ok && !ep.tma_c) continue;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -386,20 +395,22 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
 
 // Epilogue of one 128 x BN accumulator tile for one row m; warps that share a
 // lane quarter split the column chunks round-robin (part of nparts).
-template <int BN>
+template <int BN, class PS = NoPartial>
 __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, int m, int n0, int part,
                                               int nparts, const CUtensorMap* tmC, const CUtensorMap* tmR,
-                                              EpiStore& es, int lane) {
+                                              EpiStore& es, int lane, const PS& ps = PS()) {
   const bool row_ok = m < ep.M;
   const long long orow = out_row(ep, m);
   if (ep.act == VLA_ACT_ROPE) {
-    rope_tile<BN>(ep, taddr, m, n0, orow, row_ok, part, nparts, tmC, es, lane);
+    rope_tile<BN, PS>(ep, taddr, m, n0, orow, row_ok, part, nparts, tmC, es, lane, ps);
   } else if (ep.act == VLA_ACT_SWIGLU) {
 #pragma unroll 1
     for (int c = 32 * part; c < BN; c += 32 * nparts) {
       float g[16], u[16];
       tmem_ld16(taddr + c, g);
       tmem_ld16(taddr + c + 16, u);
+      ps.add16(c, g);
+      ps.add16(c + 16, u);
       const int n = n0 + c;
       if (n >= ep.N) break;
       if (!row_ok && !ep.tma_c) continue;
@@ -443,6 +454,8 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       float v[32];
       tmem_ld16(taddr + c, v);
       tmem_ld16(taddr + c + 16, v + 16);
+      ps.add16(c, v);
+      ps.add16(c + 16, v + 16);
       const bool more = c + step < BN && n + step < ep.N;
       if (more) {
         prefetch32(ep, m, n + step, row_ok, nxt);

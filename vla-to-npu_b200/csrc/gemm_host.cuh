@@ -3,6 +3,7 @@
 #pragma once
 #include "gemm.cuh"
 #include "gemm2.cuh"
+#include "gemm_splitk.cuh"
 #include "host_common.cuh"
 
 namespace vla {
@@ -156,8 +157,98 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CU
   return launch_status("gemm_bf16_tc");
 }
 
+// Largest number of co-resident clusters of S split-K CTAs (kernel<BN>), cached.
+template <int BN>
+static int max_splitk_clusters(int S) {
+  static int cached[64][kMaxSplit + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (cached[dev][S] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S * (device_info().num_sms / S));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = CfgS<BN>::smem_bytes(S - 1);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_splitk_kernel<BN>, &cfg) != cudaSuccess || n <= 0)
+      n = device_info().num_sms / S;
+    cached[dev][S] = n;
+  }
+  return cached[dev][S];
+}
+
+template <int BN>
+static int launch_splitk(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc,
+                         const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N, int64_t K, int S,
+                         cudaStream_t st) {
+  using Cf = CfgS<BN>;
+  CUtensorMap tb;
+  int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
+  if (rc) return rc;
+  const int smem = Cf::smem_bytes(S - 1);
+  const int stages = Cf::stages_for(S - 1);
+  VLA_CHECK_ARG(stages >= 2, "gemm split-K: %d partial slots leave no room for the stage ring", S - 1);
+  static thread_local int attr_smem[32] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_smem[dev & 31] < smem) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_splitk_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_smem[dev & 31] = smem;
+  }
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int clusters = max_splitk_clusters<BN>(S);
+  const int grid = S * (int)(tiles < clusters ? tiles : clusters);
+  prof_begin(st);
+  launch_k_cluster(gemm_bf16_splitk_kernel<BN>, S, dim3(grid), dim3(kThreads), smem, st, ta, tb, tc, tr, ep, (int)M,
+                   (int)N, (int)K, S, stages);
+  {
+    const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
+    double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
+    if (ep.residual) bytes += 2.0 * M * out_cols;
+    if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, -S);
+  }
+  return launch_status("gemm_bf16_splitk");
+}
+
+// K split for a one-CTA tiling with few tiles: enough clusters of S CTAs to
+// cover the SMs, each CTA keeping at least two k-blocks (0 = no split).
+// Largest split whose partial slots leave room for a two-stage ring at width bn.
+static int max_split(int bn) {
+  auto fits = [&](int S) {
+    switch (bn) {
+      case 32: return CfgS<32>::stages_for(S - 1) >= 2;
+      case 64: return CfgS<64>::stages_for(S - 1) >= 2;
+      case 128: return CfgS<128>::stages_for(S - 1) >= 2;
+      default: return false;
+    }
+  };
+  int S = kMaxSplit;
+  while (S >= 2 && !fits(S)) --S;
+  return S;
+}
+
+static int choose_split(int64_t M, int64_t N, int64_t K, int bn, int num_sms) {
+  if (bn != 32 && bn != 64 && bn != 128) return 0;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  const int64_t kb = (K + BK - 1) / BK;
+  if (2 * tiles > num_sms || kb < 4) return 0;
+  int64_t S = num_sms / tiles;
+  if (S > max_split(bn)) S = max_split(bn);
+  if (S > kb / 2) S = kb / 2;
+  return S >= 2 ? (int)S : 0;
+}
+
 static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
-               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0, int force_ctas = 0) {
+               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0, int force_ctas = 0,
+               int force_split = -1) {
   VLA_CHECK_ARG(A && B && C, "gemm: null operand");
   VLA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
                 (long long)K);
@@ -254,6 +345,32 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   const int ctas = force_ctas                          ? force_ctas
                    : (env_ctas == 1 || env_ctas == 2) ? env_ctas
                                                       : choose_ctas(M, bn);
+  if (ctas == 1) {
+    // explicit splits come from vla_gemm_bf16_split
+    static const int env_split = [] {
+      const char* v = getenv("VLA_GEMM_SPLITK");
+      return v ? atoi(v) : -1;
+    }();
+    // The automatic choice does not split: inside a CUDA graph at one observation
+    // the clustered launch measured slower than the plain one on every expert
+    // shape (M = 50: 720 x 2048 12.0 -> 15.5 us, 720 x 960 7.2 -> 14.2 us,
+    // 1600 x 720 7.5 -> 14.6 us; the whole B = 1 chunk 10.0 -> 13.4 ms), the
+    // per-launch cost of these tiny GEMMs being fixed overhead, not the K loop.
+    // VLA_GEMM_SPLITK=1 enables choose_split for measurements.
+    int split = force_split >= 0 ? force_split
+                : env_split == 1 ? choose_split(M, N, K, bn, device_info().num_sms)
+                                 : 0;
+    if (split > kMaxSplit || (split >= 2 && (K + BK - 1) / BK < split))
+      return set_error(VLA_E_INVALID, "gemm: split %d needs 2..%d and at most one part per k-block", split, kMaxSplit);
+    if (split >= 2) {
+      switch (bn) {
+        case 32: return launch_splitk<32>(ta, B, ldb, tc, tr, ep, M, N, K, split, st);
+        case 64: return launch_splitk<64>(ta, B, ldb, tc, tr, ep, M, N, K, split, st);
+        case 128: return launch_splitk<128>(ta, B, ldb, tc, tr, ep, M, N, K, split, st);
+        default: return set_error(VLA_E_UNSUPPORTED, "gemm: split-K tile width %d not built", bn);
+      }
+    }
+  }
   if (ctas == 2 && !force_bn) bn = choose_bn_pair(M, N, act, device_info().num_sms);
   if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
   if (ctas == 2) {

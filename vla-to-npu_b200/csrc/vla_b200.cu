@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "blocks.cuh"
+#include "render.cuh"
 #include "gemm_host.cuh"
 #include "host_common.cuh"
 
@@ -156,6 +157,16 @@ int vla_gemm_bf16_ex(const void* A, int64_t lda, const void* B, int64_t ldb, voi
   return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n, ctas);
 }
 
+int vla_gemm_bf16_split(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M,
+                        int64_t N, int64_t K, const vla_epilogue* epi, int32_t tile_n, int32_t splits,
+                        vla_stream_t stream) {
+  VLA_CHECK_ARG(splits == 0 || splits == 1 || (splits >= 2 && splits <= 8), "gemm: splits must be 0, 1 or 2..8");
+  VLA_CHECK_ARG(tile_n == 0 || tile_n == 32 || tile_n == 64 || tile_n == 128,
+                "gemm split-K: tile_n must be 0, 32, 64 or 128");
+  return gemm::run(A, lda, B, ldb, C, ldc, M, N, K, epi, as_stream(stream), tile_n, 1,
+                   splits == 0 ? -1 : splits == 1 ? 0 : splits);
+}
+
 int vla_rms_norm_bf16(const void* x, int64_t ldx, const void* g, void* y, int64_t ldy, int64_t M, int64_t N, float eps,
                       vla_stream_t stream) {
   return blocks::rownorm(0, x, ldx, g, nullptr, y, ldy, M, N, eps, as_stream(stream));
@@ -278,6 +289,17 @@ int vla_camera_preprocess_u8(const uint8_t* frames, int32_t B, int32_t H, int32_
            p, mode, (float)H / (float)S, (float)W / (float)S);
   prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, (double)B * H * W * 3 + 2.0 * B * 3 * S * S);
   return launch_status("camera_preprocess");
+}
+
+int vla_pusht_render_u8(const float* scene, int32_t n, int32_t S, uint8_t* frames, vla_stream_t stream) {
+  VLA_CHECK_ARG(scene && frames && n >= 0 && S > 0, "pusht_render: bad arguments");
+  if (n == 0) return VLA_OK;
+  const long long work = (long long)n * S * S;
+  prof_begin(as_stream(stream));
+  launch_k(render::pusht_render_kernel, dim3(blocks::grid_for(work, 256)), dim3(256), 0, as_stream(stream), scene, n,
+           S, frames);
+  prof_end(as_stream(stream), VLA_KIND_LAYOUT, 0.0, 3.0 * (double)work);
+  return launch_status("pusht_render");
 }
 
 int vla_patch_im2col_bf16(const void* img, void* out, int32_t B, int32_t Cin, int32_t H, int32_t W, int32_t p,

@@ -132,6 +132,7 @@ SIGNATURES = {
     "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
     "vla_gemm_bf16_tiled": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _P],
     "vla_gemm_bf16_ex": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _I32, _P],
+    "vla_gemm_bf16_split": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _I32, _I32, _P],
     "vla_rms_norm_bf16": [_P, _I64, _P, _P, _I64, _I64, _I64, _F32, _P],
     "vla_layer_norm_bf16": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _F32, _P],
     "vla_rope_bf16": [_P, _I64, _I64, _I32, _I32, _P, _P],
@@ -143,6 +144,7 @@ SIGNATURES = {
     "vla_patch_im2col_bf16": [_P, _P, _I32, _I32, _I32, _I32, _I32, _P],
     "vla_embed_bf16": [_P, _P, _I32, _I32, _I32, _I32, _F32, _P, _I64, _I32, _I32, _P],
     "vla_f32_to_bf16": [_P, _I64, _P, _I64, _I64, _I64, _P],
+    "vla_pusht_render_u8": [_P, _I32, _I32, _P, _P],
     "vla_camera_preprocess_u8": [_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P],
     "vla_llama_layer_workspace": [ctypes.POINTER(LlamaLayer), _I64, _I32],
     "vla_llama_self_layer_bf16": [ctypes.POINTER(LlamaLayer), _P, _I32, _I32, _P, _P, _P, ctypes.c_size_t, _P],

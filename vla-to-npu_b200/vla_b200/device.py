@@ -52,8 +52,9 @@ def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, al
 
 
 def gemm(a: torch.Tensor, w_t: torch.Tensor, out: torch.Tensor, epi: Optional[Epilogue] = None, m: Optional[int] = None,
-         tile_n: int = 0, ctas: int = 0) -> torch.Tensor:
-    """out = epilogue(a @ w_t.T) with a [M, K] and w_t [N, K] (K-major weights)."""
+         tile_n: int = 0, ctas: int = 0, splits: Optional[int] = None) -> torch.Tensor:
+    """out = epilogue(a @ w_t.T) with a [M, K] and w_t [N, K] (K-major weights).
+    ``splits`` (one-CTA tiles only) forces the K split: 1 = none, 2..8 CTAs per tile."""
     lda = _rowmajor(a, "a")
     ldb = _rowmajor(w_t, "w_t")
     ldc = _rowmajor(out, "out")
@@ -62,7 +63,10 @@ def gemm(a: torch.Tensor, w_t: torch.Tensor, out: torch.Tensor, epi: Optional[Ep
     if a.shape[1] != K:
         raise ValueError(f"gemm: a has K={a.shape[1]}, w_t has K={K}")
     ep = ctypes.byref(epi) if epi is not None else None
-    if ctas:
+    if splits is not None:
+        _lib.call("vla_gemm_bf16_split", _ptr(a), lda, _ptr(w_t), ldb, _ptr(out), ldc, M, N, K, ep, tile_n, splits,
+                  _stream())
+    elif ctas:
         _lib.call("vla_gemm_bf16_ex", _ptr(a), lda, _ptr(w_t), ldb, _ptr(out), ldc, M, N, K, ep, tile_n, ctas,
                   _stream())
     elif tile_n:
