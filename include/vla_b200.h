@@ -110,6 +110,14 @@ uint64_t vla_launch_count(void);
  * global-memory access).  On by default; 0 disables it.  Returns the previous
  * setting.  No counterpart in the reference (its NPU calls are synchronous). */
 int vla_set_launch_overlap(int32_t enable);
+/* Single-launch layers: a vla_llama_self_layer_bf16 / vla_llama_cross_layer_bf16
+ * call of at most 512 rows (batch * seq) with at most 128 keys runs the whole
+ * layer (two RMSNorms, four GEMMs, attention) as ONE cooperative kernel, one CTA
+ * per SM, its phases separated by grid-wide barriers, instead of seven
+ * dependent launches (single-observation inference is launch-bound).  On by
+ * default; 0 selects the seven-launch path.  Returns the previous setting.  No
+ * counterpart in the reference (its layers are sequences of NPU calls). */
+int vla_set_fused_layers(int32_t enable);
 
 /* Launch profiler (measurement only; no counterpart in the reference, whose
  * timing is the XRT host's "NPU execution time" print, gemm/v1_test_tiled_gemm.py:81-96).

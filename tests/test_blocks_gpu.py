@@ -229,3 +229,48 @@ def test_infer_overlapped_matches_per_batch(cuda):
         m.infer_overlapped(batches, outs)
         for o, r in zip(outs, refs):
             assert torch.equal(o, r)
+
+
+@pytest.mark.parametrize("kind,B,L", [("text", 1, 128), ("text", 2, 113), ("self", 3, 50), ("cross", 3, 50),
+                                      ("self", 8, 50)])
+def test_fused_layer_matches_seven_launch_layer(cuda, kind, B, L):
+    """The single-launch layer (cooperative kernel, grid barriers between its seven
+    phases) against the seven-launch layer on the same inputs: the same kernels'
+    arithmetic in the same order, so the outputs agree to the last bit or within
+    one bf16 rounding of an attention row."""
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    from vla_b200.model import LlamaLayerWeights, rope_table
+    lib = _lib.load()
+    t, e = TextCfg(), ExpertCfg()
+    cfg = t if kind == "text" else e
+    if kind == "cross":
+        p = W.expert_cross_params(e, t.kv_dim, seed=31, layer=1)
+    elif kind == "self":
+        p = W.expert_self_params(e, seed=31)
+    else:
+        p = W.text_block_params(t, seed=31)
+    lw = LlamaLayerWeights(p, cfg, "cuda", cross=kind == "cross")
+    x0 = _x((B * L, cfg.hidden), 31, "fused.x").to(BF).cuda()
+    cs = rope_table(L, 64, cfg.rope_theta).cuda()
+    kv = _x((B * 113, 2 * e.kv_dim), 31, "fused.kv").to(BF).cuda()
+    kv_len = torch.tensor([113, 97, 64][:B], dtype=torch.int32, device="cuda")
+    outs = {}
+    try:
+        for fused in (1, 0):
+            lib.vla_set_fused_layers(fused)
+            x = x0.clone()
+            qkv = torch.empty(B * L, cfg.q_dim + 2 * cfg.kv_dim, dtype=BF, device="cuda")
+            if kind == "cross":
+                dev.llama_cross_layer(lw.struct, x, B, L, cs, kv[:, :e.kv_dim], kv[:, e.kv_dim:], 113, dev.Workspace(),
+                                      kv_len=kv_len)
+            else:
+                dev.llama_self_layer(lw.struct, x, B, L, cs, dev.Workspace(), qkv_out=qkv)
+            dev.sync_check()
+            outs[fused] = (x, qkv)
+    finally:
+        lib.vla_set_fused_layers(1)
+    torch.testing.assert_close(outs[1][0].float(), outs[0][0].float(), atol=2e-2, rtol=1e-2)
+    if kind != "cross":
+        assert torch.equal(outs[1][1], outs[0][1]), "Q / K / V differ"
+    print(f"[fused] {kind} B={B} L={L}: bit-identical output = {torch.equal(outs[1][0], outs[0][0])}")

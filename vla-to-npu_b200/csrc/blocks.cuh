@@ -8,6 +8,7 @@
 #include "attention_tc.cuh"
 #include "elementwise.cuh"
 #include "gemm_host.cuh"
+#include "layer_fused.cuh"
 #include "norm.cuh"
 
 namespace vla {
@@ -264,6 +265,7 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl
 // ----------------------------------------------------------------------------
 struct LlamaWs {
   bf16 *h, *qkv, *attn, *mlp;
+  unsigned int* counter;
 };
 
 // Layer calls take rows = batch * seq below 2^31 (the GEMM's M limit); checking
@@ -277,7 +279,7 @@ static size_t llama_ws_bytes(const vla_llama_layer* w, int64_t rows, bool need_q
   const int64_t q = (int64_t)w->heads * w->head_dim, kv = (int64_t)w->kv_heads * w->head_dim;
   size_t s = align_up(rows * w->hidden * 2) + align_up(rows * q * 2) + align_up(rows * w->ffn * 2);
   if (need_qkv) s += align_up(rows * (q + 2 * kv) * 2);
-  return s;
+  return s + 256;  // the fused layer kernel's grid-barrier counter
 }
 
 static LlamaWs carve(const vla_llama_layer* w, int64_t rows, void* ws, bool need_qkv) {
@@ -290,7 +292,11 @@ static LlamaWs carve(const vla_llama_layer* w, int64_t rows, void* ws, bool need
   p += align_up(rows * q * 2);
   r.mlp = (bf16*)p;
   p += align_up(rows * w->ffn * 2);
-  if (need_qkv) r.qkv = (bf16*)p;
+  if (need_qkv) {
+    r.qkv = (bf16*)p;
+    p += align_up(rows * (q + 2 * (int64_t)w->kv_heads * w->head_dim) * 2);
+  }
+  r.counter = (unsigned int*)p;
   return r;
 }
 
@@ -318,6 +324,117 @@ static int llama_mlp(const vla_llama_layer* w, bf16* x, int64_t rows, const Llam
   return gemm::run(ws.mlp, F, w->w_down, F, x, H, rows, H, F, &r, st);
 }
 
+// The whole layer as one cooperative launch (layer_fused.cuh) for small row
+// counts, where seven dependent launches would cost more than their work.
+static constexpr int64_t kFusedLayerRows = 512;
+
+static std::atomic<int> g_fused_layers{1};  // vla_set_fused_layers()
+
+static bool use_fused_layer(const vla_llama_layer* w, int64_t rows, int kv_seq) {
+  return g_fused_layers.load(std::memory_order_relaxed) != 0 && rows <= kFusedLayerRows && kv_seq >= 1 && kv_seq <= 128 && w->hidden <= 1024 &&
+         w->hidden % 8 == 0 && w->heads % w->kv_heads == 0;
+}
+
+static int llama_fused(const vla_llama_layer* w, bf16* x, int batch, int seq, const float* rope_cs, bf16* qkv,
+                       const bf16* k, const bf16* v, int64_t ldkv, int kv_seq, const int* kv_len, const LlamaWs& b,
+                       bool cross, cudaStream_t st) {
+  const int64_t rows = (int64_t)batch * seq, H = w->hidden, F = w->ffn;
+  const int64_t Q = (int64_t)w->heads * 64, KV = (int64_t)w->kv_heads * 64;
+  const int64_t NQ = cross ? Q : Q + 2 * KV;
+  lfused::Params P;
+  memset(&P, 0, sizeof(P));
+  gemm::GemmPlan pq, po, pg, pd;
+  vla_epilogue e{};
+  e.act = VLA_ACT_ROPE;
+  e.rope_cs = rope_cs;
+  e.rope_seq = seq;
+  e.rope_ncols = (int)(cross ? Q : Q + KV);
+  int rc = gemm::plan_gemm(b.h, H, w->w_qkv, H, qkv, NQ, rows, NQ, H, &e, pq);
+  vla_epilogue r{};
+  r.residual = x;
+  r.ldr = H;
+  if (!rc) rc = gemm::plan_gemm(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, po);
+  vla_epilogue g{};
+  g.act = VLA_ACT_SWIGLU;
+  if (!rc) rc = gemm::plan_gemm(b.h, H, w->w_gu, H, b.mlp, F, rows, 2 * F, H, &g, pg);
+  if (!rc) rc = gemm::plan_gemm(b.mlp, F, w->w_down, F, x, H, rows, H, F, &r, pd);
+  if (!rc) rc = make_tmap_bf16_2d(&P.b_qkv, w->w_qkv, (uint64_t)H, (uint64_t)NQ, (uint64_t)H, gemm::BK, 64);
+  if (!rc) rc = make_tmap_bf16_2d(&P.b_o, w->w_o, (uint64_t)Q, (uint64_t)H, (uint64_t)Q, gemm::BK, 32);
+  if (!rc) rc = make_tmap_bf16_2d(&P.b_gu, w->w_gu, (uint64_t)H, (uint64_t)(2 * F), (uint64_t)H, gemm::BK, 32);
+  if (!rc) rc = make_tmap_bf16_2d(&P.b_down, w->w_down, (uint64_t)F, (uint64_t)H, (uint64_t)F, gemm::BK, 32);
+  if (rc) return rc;
+  P.a_h = pq.ta;
+  P.a_attn = po.ta;
+  P.a_mlp = pd.ta;
+  P.c_qkv = pq.tc;
+  P.c_x = po.tc;
+  P.r_x = po.tr;
+  P.c_mlp = pg.tc;
+  P.g_qkv = {pq.ep, (int)rows, (int)NQ, (int)H};
+  P.g_o = {po.ep, (int)rows, (int)H, (int)Q};
+  P.g_gu = {pg.ep, (int)rows, (int)(2 * F), (int)H};
+  P.g_down = {pd.ep, (int)rows, (int)H, (int)F};
+  P.norm1 = (const bf16*)w->norm1;
+  P.norm2 = (const bf16*)w->norm2;
+  P.x = x;
+  P.h = b.h;
+  P.rows = (int)rows;
+  P.H = (int)H;
+  P.eps = w->eps;
+  attn_sq::Params& a = P.att;
+  a.q = qkv;
+  a.k = cross ? k : qkv + Q;
+  a.v = cross ? v : qkv + Q + KV;
+  a.o = b.attn;
+  a.q_row = NQ;
+  a.q_batch = (long long)seq * NQ;
+  a.k_row = a.v_row = cross ? ldkv : NQ;
+  a.k_batch = a.v_batch = cross ? (long long)kv_seq * ldkv : (long long)seq * NQ;
+  a.o_row = Q;
+  a.o_batch = (long long)seq * Q;
+  a.Lq = seq;
+  a.Lk = kv_seq;
+  a.Hq = w->heads;
+  a.Hkv = w->kv_heads;
+  a.G = w->heads / w->kv_heads;
+  a.n_mt = (a.G * seq + attn_sq::MT - 1) / attn_sq::MT;
+  a.batch = batch;
+  a.causal = cross ? 0 : 1;
+  a.kv_len = cross ? kv_len : nullptr;
+  a.scale_log2 = 0.125f * 1.4426950408889634f;
+  P.barrier = b.counter;
+  VLA_CUDA_TRY(cudaMemsetAsync(b.counter, 0, sizeof(unsigned int), st));
+  auto kern = kv_seq <= 64 ? lfused::llama_layer_fused_kernel<64> : lfused::llama_layer_fused_kernel<128>;
+  static thread_local int attr_dev_mask[2] = {0, 0};
+  const int which = kv_seq <= 64 ? 0 : 1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask[which] & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lfused::SMEM_BYTES));
+    int per_sm = 0;
+    VLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, gemm::kThreads, lfused::SMEM_BYTES));
+    if (per_sm < 1) return set_error(VLA_E_CUDA, "fused layer: no resident CTA per SM");
+    attr_dev_mask[which] |= 1 << (dev & 31);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(device_info().num_sms);
+  cfg.blockDim = dim3(gemm::kThreads);
+  cfg.dynamicSmemBytes = lfused::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  prof_begin(st);
+  cudaLaunchKernelEx(&cfg, kern, P);
+  prof_end(st, VLA_KIND_GEMM,
+           2.0 * rows * ((double)NQ * H + (double)H * Q + 2.0 * F * H + (double)H * F) +
+               4.0 * batch * w->heads * (double)seq * kv_seq * 64,
+           2.0 * ((double)NQ * H + (double)H * Q + 2.0 * F * H + (double)H * F));
+  return launch_status("llama_layer_fused");
+}
+
 static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, const float* rope_cs, void* qkv_out,
                       void* ws, size_t ws_bytes, cudaStream_t st) {
   int rc = check_llama(w);
@@ -335,6 +452,8 @@ static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, co
   bf16* x = (bf16*)xv;
   bf16* qkv = own_qkv ? b.qkv : (bf16*)qkv_out;
   const int64_t H = w->hidden, Q = (int64_t)w->heads * 64, KV = (int64_t)w->kv_heads * 64, NQKV = Q + 2 * KV;
+  if (use_fused_layer(w, rows, seq))
+    return llama_fused(w, x, batch, seq, rope_cs, qkv, nullptr, nullptr, 0, seq, nullptr, b, false, st);
 
   rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
   if (rc) return rc;
@@ -386,6 +505,9 @@ static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, c
   LlamaWs b = carve(w, rows, ws, true);
   bf16* x = (bf16*)xv;
   bf16* q = b.qkv;  // [rows, Q]
+  if (use_fused_layer(w, rows, kv_seq))
+    return llama_fused(w, x, batch, seq, rope_cs, q, (const bf16*)k, (const bf16*)v, ldkv, kv_seq, kv_len, b, true,
+                       st);
 
   rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
   if (rc) return rc;

@@ -246,9 +246,16 @@ static int choose_split(int64_t M, int64_t N, int64_t K, int bn, int num_sms) {
   return S >= 2 ? (int)S : 0;
 }
 
-static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
-               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0, int force_ctas = 0,
-               int force_split = -1) {
+// Everything of a GEMM launch but the tile width: argument checks, the device
+// epilogue description and the A / C / residual tensor maps.
+struct GemmPlan {
+  DevEpi ep;
+  int act;
+  CUtensorMap ta, tc, tr;
+};
+
+static int plan_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
+                     int64_t K, const vla_epilogue* e, GemmPlan& plan) {
   VLA_CHECK_ARG(A && B && C, "gemm: null operand");
   VLA_CHECK_ARG(M >= 0 && N > 0 && K > 0, "gemm: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
                 (long long)K);
@@ -257,15 +264,17 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   VLA_CHECK_ARG(lda >= K && ldb >= K, "gemm: lda/ldb smaller than K");
   VLA_CHECK_ALIGN(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0, "gemm: lda/ldb/ldc must be multiples of 8 elements");
   VLA_CHECK_ALIGN(aligned16(A) && aligned16(B) && aligned16(C), "gemm: A/B/C must be 16-byte aligned");
-  if (M == 0) return VLA_OK;
+  if (M == 0) return VLA_OK;  // nothing to launch; the plan stays unfilled
 
-  DevEpi ep{};
+  DevEpi& ep = plan.ep;
+  ep = DevEpi{};
   ep.C = reinterpret_cast<bf16*>(C);
   ep.ldc = ldc;
   ep.alpha = 1.f;
   ep.M = (int)M;
   ep.N = (int)N;
-  int act = VLA_ACT_NONE;
+  int& act = plan.act;
+  act = VLA_ACT_NONE;
   if (e != nullptr) {
     act = e->act;
     ep.bias = reinterpret_cast<const bf16*>(e->bias);
@@ -305,14 +314,14 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
     VLA_CHECK_ALIGN(aligned16(ep.euler_x) && ep.ldx % 4 == 0, "gemm: Euler state must be 16-byte aligned");
   }
 
-  CUtensorMap ta;
+  CUtensorMap& ta = plan.ta;
   int rc = make_tmap_bf16_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM);
   if (rc) return rc;
   // Output through shared memory + TMA stores for the plain / bias / GELU /
   // residual / SwiGLU / RoPE epilogues (row scatter and Euler store directly).
   // Box: 32 rows x 32 columns (64-byte swizzle), or 16 columns (32-byte
   // swizzle); out-of-range rows and columns are clipped.
-  CUtensorMap tc;
+  CUtensorMap& tc = plan.tc;
   memset(&tc, 0, sizeof(tc));
   ep.tma_c = (act == VLA_ACT_NONE || act == VLA_ACT_GELU_TANH || act == VLA_ACT_SWIGLU ||
               (act == VLA_ACT_ROPE && ep.residual == nullptr)) &&
@@ -326,7 +335,7 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   }
   // The residual through the same staging buffers (32 x 32 chunks, 64-byte
   // swizzle) when each 32-row block maps to 32 consecutive residual rows.
-  CUtensorMap tr;
+  CUtensorMap& tr = plan.tr;
   memset(&tr, 0, sizeof(tr));
   ep.tma_r = ep.tma_c && ep.residual != nullptr && act != VLA_ACT_SWIGLU &&
              (ep.res_row_mod == 0 || ep.res_row_mod % 32 == 0);
@@ -336,6 +345,21 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
                            CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   }
+  return VLA_OK;
+}
+
+static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, int64_t M, int64_t N,
+               int64_t K, const vla_epilogue* e, cudaStream_t st, int force_bn = 0, int force_ctas = 0,
+               int force_split = -1) {
+  GemmPlan plan;
+  int rc = plan_gemm(A, lda, B, ldb, C, ldc, M, N, K, e, plan);
+  if (rc) return rc;
+  if (M == 0) return VLA_OK;
+  const DevEpi& ep = plan.ep;
+  const int act = plan.act;
+  const CUtensorMap& ta = plan.ta;
+  const CUtensorMap& tc = plan.tc;
+  const CUtensorMap& tr = plan.tr;
   int bn = force_bn ? force_bn : choose_bn(M, N, act, device_info().num_sms);
   // VLA_GEMM_CTAS=1|2 overrides the automatic one-CTA / pair choice (A/B measurement)
   static const int env_ctas = [] {

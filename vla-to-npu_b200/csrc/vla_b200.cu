@@ -82,6 +82,8 @@ int vla_peek_device_error(unsigned int* code) {
 
 uint64_t vla_launch_count(void) { return g_launch_count.load(); }
 
+int vla_set_fused_layers(int32_t enable) { return blocks::g_fused_layers.exchange(enable ? 1 : 0); }
+
 int vla_set_launch_overlap(int32_t enable) {
   const int old = g_launch_overlap.exchange(enable ? 1 : 0);
   return old;

@@ -127,6 +127,7 @@ SIGNATURES = {
     "vla_abi_sizes": [ctypes.POINTER(ctypes.c_int64), _I32],
     "vla_launch_count": [],
     "vla_set_launch_overlap": [_I32],
+    "vla_set_fused_layers": [_I32],
     "vla_profile_start": [_I32],
     "vla_profile_stop": [ctypes.POINTER(ProfileRecord), _I32, ctypes.POINTER(ctypes.c_int32)],
     "vla_gemm_bf16": [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, ctypes.POINTER(Epilogue), _P],
