@@ -114,9 +114,12 @@ int vla_set_launch_overlap(int32_t enable);
  * call of at most 512 rows (batch * seq) with at most 128 keys runs the whole
  * layer (two RMSNorms, four GEMMs, attention) as ONE cooperative kernel, one CTA
  * per SM, its phases separated by grid-wide barriers, instead of seven
- * dependent launches (single-observation inference is launch-bound).  On by
- * default; 0 selects the seven-launch path.  Returns the previous setting.  No
- * counterpart in the reference (its layers are sequences of NPU calls). */
+ * dependent launches.  Results are bit-identical to the seven-launch path.
+ * Off by default: measured at one observation it is slower (an expert layer
+ * ~66 us against ~50 us inside a CUDA graph: each phase's TMA / MMA / store
+ * latency plus a grid barrier costs more than the launch it saves).  1 enables
+ * it, 0 disables; returns the previous setting.  No counterpart in the
+ * reference (its layers are sequences of NPU calls). */
 int vla_set_fused_layers(int32_t enable);
 
 /* Launch profiler (measurement only; no counterpart in the reference, whose

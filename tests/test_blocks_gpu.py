@@ -256,6 +256,7 @@ def test_fused_layer_matches_seven_launch_layer(cuda, kind, B, L):
     kv = _x((B * 113, 2 * e.kv_dim), 31, "fused.kv").to(BF).cuda()
     kv_len = torch.tensor([113, 97, 64][:B], dtype=torch.int32, device="cuda")
     outs = {}
+    prev = lib.vla_set_fused_layers(1)
     try:
         for fused in (1, 0):
             lib.vla_set_fused_layers(fused)
@@ -269,7 +270,7 @@ def test_fused_layer_matches_seven_launch_layer(cuda, kind, B, L):
             dev.sync_check()
             outs[fused] = (x, qkv)
     finally:
-        lib.vla_set_fused_layers(1)
+        lib.vla_set_fused_layers(prev)
     torch.testing.assert_close(outs[1][0].float(), outs[0][0].float(), atol=2e-2, rtol=1e-2)
     if kind != "cross":
         assert torch.equal(outs[1][1], outs[0][1]), "Q / K / V differ"

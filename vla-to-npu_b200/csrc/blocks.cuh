@@ -325,10 +325,13 @@ static int llama_mlp(const vla_llama_layer* w, bf16* x, int64_t rows, const Llam
 }
 
 // The whole layer as one cooperative launch (layer_fused.cuh) for small row
-// counts, where seven dependent launches would cost more than their work.
+// counts.  Off by default: at one observation it measured slower than the
+// seven launches it replaces (expert layer ~66 vs ~50 us in the graph; B = 1
+// chunk 10.4 vs 8.0 ms for the expert), the phases' own latency, not the
+// launches, being the cost.
 static constexpr int64_t kFusedLayerRows = 512;
 
-static std::atomic<int> g_fused_layers{1};  // vla_set_fused_layers()
+static std::atomic<int> g_fused_layers{0};  // vla_set_fused_layers()
 
 static bool use_fused_layer(const vla_llama_layer* w, int64_t rows, int kv_seq) {
   return g_fused_layers.load(std::memory_order_relaxed) != 0 && rows <= kFusedLayerRows && kv_seq >= 1 && kv_seq <= 128 && w->hidden <= 1024 &&

@@ -20,7 +20,10 @@
 //                 O = P V with P from TMEM), Q / K / V staged with cp.async.
 // Between phases each CTA drains its TMA stores, fences (generic and async
 // proxies) and arrives on the barrier; after it, the TMA loads of the next phase
-// see every CTA's results.  Semantics are those of the unfused layer.
+// see every CTA's results.  Semantics (and bits) are those of the unfused layer.
+// Measured at one observation it is slower than the seven launches (the
+// phases' own latency dominates), so the library uses it only on request
+// (vla_set_fused_layers).
 #pragma once
 #include "attention_short.cuh"
 #include "gemm.cuh"
