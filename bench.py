@@ -418,6 +418,112 @@ def workload_config(args, batch, world):
 # ---------------------------------------------------------------------------
 # the CUDA path
 # ---------------------------------------------------------------------------
+# The step's GEMMs with their fused epilogues: (name, M, N, K, epilogue)
+STEP_GEMMS = [
+    ("vision fc1 +bias +GELU", 262144, 3072, 768, "gelu"),
+    ("vision fc2 +bias +residual", 262144, 768, 3072, "bias_res"),
+    ("vision qkv +bias", 262144, 2304, 768, "bias"),
+    ("vision o +bias +residual", 262144, 768, 768, "bias_res"),
+    ("text gate/up SwiGLU", 28928, 5120, 960, "swiglu"),
+    ("text down +residual", 28928, 960, 2560, "res"),
+    ("text qkv RoPE", 28928, 1600, 960, "rope"),
+    ("text o +residual", 28928, 960, 960, "res"),
+    ("expert gate/up SwiGLU", 12800, 4096, 720, "swiglu"),
+    ("expert down +residual", 12800, 720, 2048, "res"),
+    ("expert qkv RoPE", 12800, 1600, 720, "rope"),
+    ("expert cross q RoPE", 12800, 960, 720, "rope"),
+    ("expert o +residual", 12800, 720, 960, "res"),
+]
+
+
+def gemm_shape_rates(peak_tflops: float, reps: int = 20) -> list:
+    """Each GEMM of the B = 256 step at its shape and epilogue, timed as a CUDA graph
+    of `reps` back-to-back launches (launch overlap between them as inside the step's
+    graph).  The launch profile's per-launch events instead cut that overlap and
+    charge each launch its ramp and tail, which costs the short expert GEMMs 30-60 %."""
+    from vla_b200 import _lib
+    from vla_b200 import device as dev
+    from vla_b200.model import rope_table
+    bf = torch.bfloat16
+    out = []
+    g = torch.Generator(device="cpu").manual_seed(5)
+    for name, M, N, K, kind in STEP_GEMMS:
+        a = (torch.randn(M, K, generator=g, dtype=torch.float32)).to(bf).cuda()
+        w = (torch.randn(N, K, generator=g, dtype=torch.float32) * 0.02).to(bf).cuda()
+        oc = N // 2 if kind == "swiglu" else N
+        c = torch.empty(M, oc, dtype=bf, device="cuda")
+        bias = torch.zeros(N, dtype=bf, device="cuda")
+        res = torch.randn(M, oc, generator=g, dtype=torch.float32).to(bf).cuda() if "res" in kind else None
+        if kind == "gelu":
+            epi = dev.make_epilogue(bias=bias, act=_lib.ACT_GELU_TANH)
+        elif kind == "bias":
+            epi = dev.make_epilogue(bias=bias)
+        elif kind == "bias_res":
+            epi = dev.make_epilogue(bias=bias, residual=res)
+        elif kind == "res":
+            epi = dev.make_epilogue(residual=res)
+        elif kind == "swiglu":
+            epi = dev.make_epilogue(act=_lib.ACT_SWIGLU)
+        else:
+            seq = 113 if M == 28928 else 50
+            cs = rope_table(seq, 64, 1e4).cuda()
+            epi = dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=seq, rope_ncols=min(N, 1280))
+        dev.gemm(a, w, c, epi)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                dev.gemm(a, w, c, epi)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+        out.append({"gemm": name, "mnk": [M, N, K], "us": round(us, 2), "tflops": round(tf, 1),
+                    "frac_of_bf16_peak": round(tf / peak_tflops, 3)})
+        del a, w, c, res, graph
+    torch.cuda.empty_cache()
+    return out
+
+
+def norm_rates(hbm_peak: float, reps: int = 20) -> list:
+    """The step's row norms at their B = 256 shapes, timed like gemm_shape_rates."""
+    from vla_b200 import device as dev
+    bf = torch.bfloat16
+    out = []
+    for name, M, N, ln in (("expert RMSNorm", 12800, 720, False), ("text RMSNorm", 28928, 960, False),
+                           ("vision LayerNorm", 262144, 768, True)):
+        x = torch.randn(M, N, device="cuda").to(bf)
+        y = torch.empty_like(x)
+        g = torch.ones(N, dtype=bf, device="cuda")
+        b = torch.zeros(N, dtype=bf, device="cuda")
+        fn = (lambda: dev.layer_norm(x, g, b, 1e-6, out=y)) if ln else (lambda: dev.rms_norm(x, g, 1e-5, out=y))
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        gbs = 4.0 * M * N / (us * 1e-6) / 1e9
+        out.append({"norm": name, "shape": [M, N], "us": round(us, 2), "gbs": round(gbs, 1),
+                    "frac_of_hbm": round(gbs / hbm_peak, 3),
+                    "l2_resident": 4.0 * M * N < 126e6})
+        del x, y, graph
+    return out
+
+
 def profile_pass(model) -> dict:
     """Eager forward under the launch profiler; the queue is pre-filled behind a
     sleep kernel so launch gaps do not enter the per-kernel device times."""
@@ -696,6 +802,20 @@ def run_ours(args, rank, world, local):
                 extras["blocks"] = block_timings(model, peaks)
             except Exception as exc:  # extras never fail the benchmark line
                 extras["blocks_error"] = repr(exc)
+            try:
+                extras["gemm_rates_graph"] = {
+                    "peak": tflops_peak, "peak_source": f"{peak_src} bf16_tflops_sustained",
+                    "note": "each step GEMM alone at the B = 256 shape and epilogue, 20 launches in one CUDA "
+                            "graph, operands L2-warm across the launches",
+                    "shapes": gemm_shape_rates(tflops_peak)}
+            except Exception as exc:
+                extras["gemm_rates_graph_error"] = repr(exc)
+            try:
+                extras["norm_rates_graph"] = {"peak_gbs": hbm_peak, "shapes": norm_rates(hbm_peak),
+                                              "note": "algorithmic bytes (read + write) over graph-replay time; "
+                                                      "shapes under L2 size stay L2-resident across the launches"}
+            except Exception as exc:
+                extras["norm_rates_graph_error"] = repr(exc)
             sweep = {}
             for b in (1, 8, 64):
                 model.allocate(b)

@@ -76,7 +76,10 @@ typedef struct vla_epilogue {
   float* euler_x;        /* fp32 [M, ldx] Euler state (VLA_ACT_EULER) */
   int64_t ldx;
   float euler_dt;
-  int32_t reserved[4];
+  /* 1 when no work earlier in the stream writes B (model weights): a one-CTA
+   * launch may then fetch its first B tiles while the previous kernel drains. */
+  int32_t b_static;
+  int32_t reserved[3];
 } vla_epilogue;
 
 /* ---------------------------------------------------------------------- */

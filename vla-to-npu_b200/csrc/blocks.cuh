@@ -315,10 +315,12 @@ static int llama_mlp(const vla_llama_layer* w, bf16* x, int64_t rows, const Llam
   int rc = rownorm(0, x, H, w->norm2, nullptr, ws.h, H, rows, H, w->eps, st);
   if (rc) return rc;
   vla_epilogue e{};
+  e.b_static = 1;
   e.act = VLA_ACT_SWIGLU;
   rc = gemm::run(ws.h, H, w->w_gu, H, ws.mlp, F, rows, 2 * F, H, &e, st);
   if (rc) return rc;
   vla_epilogue r{};
+  r.b_static = 1;
   r.residual = x;
   r.ldr = H;
   return gemm::run(ws.mlp, F, w->w_down, F, x, H, rows, H, F, &r, st);
@@ -348,16 +350,19 @@ static int llama_fused(const vla_llama_layer* w, bf16* x, int batch, int seq, co
   memset(&P, 0, sizeof(P));
   gemm::GemmPlan pq, po, pg, pd;
   vla_epilogue e{};
+  e.b_static = 1;
   e.act = VLA_ACT_ROPE;
   e.rope_cs = rope_cs;
   e.rope_seq = seq;
   e.rope_ncols = (int)(cross ? Q : Q + KV);
   int rc = gemm::plan_gemm(b.h, H, w->w_qkv, H, qkv, NQ, rows, NQ, H, &e, pq);
   vla_epilogue r{};
+  r.b_static = 1;
   r.residual = x;
   r.ldr = H;
   if (!rc) rc = gemm::plan_gemm(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, po);
   vla_epilogue g{};
+  g.b_static = 1;
   g.act = VLA_ACT_SWIGLU;
   if (!rc) rc = gemm::plan_gemm(b.h, H, w->w_gu, H, b.mlp, F, rows, 2 * F, H, &g, pg);
   if (!rc) rc = gemm::plan_gemm(b.mlp, F, w->w_down, F, x, H, rows, H, F, &r, pd);
@@ -461,6 +466,7 @@ static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, co
   rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
   if (rc) return rc;
   vla_epilogue e{};
+  e.b_static = 1;
   e.act = VLA_ACT_ROPE;
   e.rope_cs = rope_cs;
   e.rope_seq = seq;
@@ -484,6 +490,7 @@ static int llama_self(const vla_llama_layer* w, void* xv, int batch, int seq, co
   rc = attention(p, batch, st);
   if (rc) return rc;
   vla_epilogue r{};
+  r.b_static = 1;
   r.residual = x;
   r.ldr = H;
   rc = gemm::run(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, st);
@@ -515,6 +522,7 @@ static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, c
   rc = rownorm(0, x, H, w->norm1, nullptr, b.h, H, rows, H, w->eps, st);
   if (rc) return rc;
   vla_epilogue e{};
+  e.b_static = 1;
   e.act = VLA_ACT_ROPE;
   e.rope_cs = rope_cs;
   e.rope_seq = seq;
@@ -542,6 +550,7 @@ static int llama_cross(const vla_llama_layer* w, void* xv, int batch, int seq, c
   rc = attention(p, batch, st);
   if (rc) return rc;
   vla_epilogue r{};
+  r.b_static = 1;
   r.residual = x;
   r.ldr = H;
   rc = gemm::run(b.attn, Q, w->w_o, Q, x, H, rows, H, Q, &r, st);
@@ -585,6 +594,7 @@ static int vision_layer(const vla_vision_layer* w, void* xv, int batch, int seq,
   int rc = rownorm(1, x, H, w->ln1_g, w->ln1_b, h, H, rows, H, w->eps, st);
   if (rc) return rc;
   vla_epilogue e{};
+  e.b_static = 1;
   e.bias = w->b_qkv;
   rc = gemm::run(h, H, w->w_qkv, H, qkv, 3 * H, rows, 3 * H, H, &e, st);
   if (rc) return rc;
@@ -604,6 +614,7 @@ static int vision_layer(const vla_vision_layer* w, void* xv, int batch, int seq,
   rc = attention(p, batch, st);
   if (rc) return rc;
   vla_epilogue r{};
+  r.b_static = 1;
   r.bias = w->b_o;
   r.residual = x;
   r.ldr = H;
@@ -612,11 +623,13 @@ static int vision_layer(const vla_vision_layer* w, void* xv, int batch, int seq,
   rc = rownorm(1, x, H, w->ln2_g, w->ln2_b, h, H, rows, H, w->eps, st);
   if (rc) return rc;
   vla_epilogue g{};
+  g.b_static = 1;
   g.bias = w->b_fc1;
   g.act = VLA_ACT_GELU_TANH;
   rc = gemm::run(h, H, w->w_fc1, H, mlp, F, rows, F, H, &g, st);
   if (rc) return rc;
   vla_epilogue d{};
+  d.b_static = 1;
   d.bias = w->b_fc2;
   d.residual = x;
   d.ldr = H;

@@ -290,6 +290,7 @@ static int plan_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, voi
     ep.euler_x = e->euler_x;
     ep.ldx = e->ldx;
     ep.euler_dt = e->euler_dt;
+    ep.b_static = e->b_static != 0;
   }
   ep.act = act;
   VLA_CHECK_ARG(act >= VLA_ACT_NONE && act <= VLA_ACT_EULER, "gemm: unknown act %d", act);

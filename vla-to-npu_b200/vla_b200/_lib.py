@@ -53,7 +53,7 @@ class Epilogue(ctypes.Structure):
         ("euler_x", ctypes.c_void_p),
         ("ldx", ctypes.c_int64),
         ("euler_dt", ctypes.c_float),
-        ("reserved", ctypes.c_int32 * 4),
+        ("b_static", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3),
     ]
 
 

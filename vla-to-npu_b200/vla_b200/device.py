@@ -32,7 +32,9 @@ def _rowmajor(t: torch.Tensor, name: str) -> int:
 
 
 def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, alpha=1.0, rope_cs=None, rope_seq=0,
-                  rope_ncols=0, out_grp=0, out_grp_stride=0, euler_x=None, euler_dt=0.0) -> Epilogue:
+                  rope_ncols=0, out_grp=0, out_grp_stride=0, euler_x=None, euler_dt=0.0, b_static=False) -> Epilogue:
+    """``b_static``: B is a weight no earlier work in the stream writes (its first
+    tiles may be fetched while the previous kernel drains)."""
     e = Epilogue()
     e.bias = None if bias is None else bias.data_ptr()
     e.residual = None if residual is None else residual.data_ptr()
@@ -48,6 +50,7 @@ def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, al
     e.euler_x = None if euler_x is None else euler_x.data_ptr()
     e.ldx = 0 if euler_x is None else _rowmajor(euler_x, "euler_x")
     e.euler_dt = euler_dt
+    e.b_static = 1 if b_static else 0
     return e
 
 

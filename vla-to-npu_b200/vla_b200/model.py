@@ -185,8 +185,8 @@ class ActionExpert:
         e = self.cfg.expert
         lw = self.layers[layer]
         kvc = self.kv_cross[self.cross_index[layer]]
-        dev.gemm(k, lw.wk_cross, kvc[:, :e.kv_dim])
-        dev.gemm(v, lw.wv_cross, kvc[:, e.kv_dim:])
+        dev.gemm(k, lw.wk_cross, kvc[:, :e.kv_dim], dev.make_epilogue(b_static=True))
+        dev.gemm(v, lw.wv_cross, kvc[:, e.kv_dim:], dev.make_epilogue(b_static=True))
 
     def set_kv_len(self, kv_len: Optional[torch.Tensor]) -> None:
         """Key-padding lengths per observation (None: every prefix key is valid).
@@ -205,7 +205,7 @@ class ActionExpert:
         dev.f32_to_bf16(self.x_t, self.x_b)
         dt = -1.0 / e.steps
         for s in range(e.steps):
-            dev.gemm(self.x_b, self.w_in, self.h, dev.make_epilogue(bias=self.temb[s]))
+            dev.gemm(self.x_b, self.w_in, self.h, dev.make_epilogue(bias=self.temb[s], b_static=True))
             for i, lw in enumerate(self.layers):
                 if lw.cross:
                     kvc = self.kv_cross[self.cross_index[i]]
@@ -215,7 +215,7 @@ class ActionExpert:
                     dev.llama_self_layer(lw.struct, self.h, B, e.chunk, self.rope, self.ws)
             dev.rms_norm(self.h, self.exp_norm, e.eps, out=self.hn)
             dev.gemm(self.hn, self.w_out, self.x_b,
-                     dev.make_epilogue(act=_lib.ACT_EULER, euler_x=self.x_t, euler_dt=dt))
+                     dev.make_epilogue(act=_lib.ACT_EULER, euler_x=self.x_t, euler_dt=dt, b_static=True))
         return self.x_t
 
     def infer(self, noise: torch.Tensor, prefix_k: torch.Tensor, prefix_v: torch.Tensor,
@@ -315,14 +315,14 @@ class SmolVLA:
         else:
             dev.patch_im2col(self.in_images, v.patch, self.patches)
         dev.gemm(self.patches, self.w_patch, self.x_vis,
-                 dev.make_epilogue(bias=self.b_patch, residual=self.pos_emb, res_row_mod=v.tokens))
+                 dev.make_epilogue(bias=self.b_patch, residual=self.pos_emb, res_row_mod=v.tokens, b_static=True))
         for lw in self.vision:
             dev.vision_layer(lw.struct, self.x_vis, B, v.tokens, self.ws)
         dev.layer_norm(self.x_vis, self.post_g, self.post_b, v.eps, out=self.x_ln)
         dev.pixel_shuffle(self.x_ln, B, v.grid, cfg.connector.scale, self.shuffled)
         # connector rows of observation b land in prefix rows [b*113, b*113 + 64)
         dev.gemm(self.shuffled, self.w_conn, self.prefix,
-                 dev.make_epilogue(out_grp=pf.image_tokens, out_grp_stride=pf.length))
+                 dev.make_epilogue(out_grp=pf.image_tokens, out_grp_stride=pf.length, b_static=True))
 
     def prefix_tokens(self) -> None:
         t, pf = self.cfg.text, self.cfg.prefix
@@ -331,7 +331,7 @@ class SmolVLA:
         # state projection -> row 112 of each observation (row stride = prefix length)
         state_rows = self.prefix[pf.image_tokens + pf.text_tokens:].as_strided(
             (self.batch, t.hidden), (pf.length * t.hidden, 1))
-        dev.gemm(self.in_state, self.w_state, state_rows)
+        dev.gemm(self.in_state, self.w_state, state_rows, dev.make_epilogue(b_static=True))
 
     def text_layers(self) -> None:
         t, pf = self.cfg.text, self.cfg.prefix
