@@ -236,7 +236,7 @@ def gather_floats(vals, world: int) -> list:
     return [o.tolist() for o in outs]
 
 
-def strong_scaling(model, dev_in, world, global_batches=(64, 256), reps=10) -> dict:
+def strong_scaling(model, dev_in, world, global_batches=(8, 64, 256), reps=10) -> dict:
     """Fixed global batch split evenly across the ranks (benchmark configuration
     C4: B observations sharded by batch over the GPUs): chunks/s of the whole job,
     timed per rank with CUDA events over graph replays, max over ranks."""

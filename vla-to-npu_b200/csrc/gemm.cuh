@@ -50,6 +50,8 @@ struct DevEpi {
   long long ldx;
   float euler_dt;
   int b_static;  // B is not written by earlier work in the stream (prefetched before the PDL wait)
+  int a_rows;    // rows of each A copy (0 = BM); 64 when M <= 64: the MMA still reads BM rows,
+                 // the rows past 64 are stale shared memory whose outputs (rows >= M) are never stored
   int tma_c;  // stores go through shared memory and the C tensor map
   int tma_r;  // the residual arrives in the same staging buffers through its tensor map
   int M, N;
@@ -524,11 +526,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // tiles of its first tile's first k-blocks before waiting for that kernel
   // (their stages are armed for the full A + B bytes; A follows after the wait).
   int prefetched = 0;
+  const uint32_t stage_tx = (uint32_t)((ep.a_rows > 0 ? ep.a_rows : BM) * BK * 2 + Cf::B_BYTES);
   if (warp == 0 && lane == 0 && ep.b_static && (int)blockIdx.x < num_tiles) {
     int mb, nb;
     tile_coords(blockIdx.x, num_m, num_n, mb, nb);
     for (; prefetched < STAGES && prefetched < num_kb; ++prefetched) {
-      mbar_arrive_expect_tx(&full[prefetched], Cf::STAGE_BYTES);
+      mbar_arrive_expect_tx(&full[prefetched], stage_tx);
       tma_load_2d(sB + prefetched * Cf::B_BYTES, &tmB, &full[prefetched], prefetched * BK, nb * BN);
     }
   }
@@ -553,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[s], stage_tx);
           tma_load_2d(sA + s * Cf::A_BYTES, &tmA, &full[s], kb * BK, mb * BM);
           tma_load_2d(sB + s * Cf::B_BYTES, &tmB, &full[s], kb * BK, nb * BN);
           ++it;

@@ -410,6 +410,13 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
       default: return set_error(VLA_E_UNSUPPORTED, "gemm: pair tile width %d not built", bn);
     }
   }
+  if (M <= 64) {
+    // one M-tile of at most 64 real rows: copy 64-row A boxes (half the A bytes
+    // of every k-block, which dominate a skinny GEMM's loads)
+    rc = make_tmap_bf16_2d(&plan.ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 64);
+    if (rc) return rc;
+    plan.ep.a_rows = 64;
+  }
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);
     case 224: return launch_bn<224>(ta, B, ldb, tc, tr, ep, M, N, K, st);
