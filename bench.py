@@ -835,6 +835,20 @@ def run_ours(args, rank, world, local):
                 sweep[str(b)] = round(b / (a_.elapsed_time(b_) / reps / 1e3), 2)
             sweep[str(B)] = round(B / (ms / 1e3), 2)
             extras["batch_sweep_chunks_per_s"] = sweep
+            # a stream of small batches through the overlapped host API: batch k+1's
+            # vision / text half runs beside batch k's action expert
+            ov = {}
+            for b in (1, 8):
+                hb = [(host["images"][i * b:(i + 1) * b].pin_memory(), host["token_ids"][i * b:(i + 1) * b].pin_memory(),
+                       host["state"][i * b:(i + 1) * b].pin_memory(), host["noise"][i * b:(i + 1) * b].pin_memory())
+                      for i in range(20)]
+                hout = [torch.empty(b, cfg.expert.chunk, cfg.expert.action_dim).pin_memory() for _ in range(20)]
+                model.infer_overlapped(hb[:3], hout[:3])
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                model.infer_overlapped(hb, hout)
+                ov[str(b)] = round(20 * b / (time.perf_counter() - t0), 2)
+            extras["stream_overlapped_chunks_per_s"] = ov
             # where one observation's chunk spends its time: the launch profile at B = 1
             try:
                 model.allocate(1)

@@ -84,6 +84,26 @@ def test_smolvla_c4_full_batch(cuda):
         check(out[b], ref32[j], refbf[j], f"C4 B=256 observation {b}")
 
 
+@pytest.mark.parametrize("B,pick", [(1, [0]), (8, [0, 7])])
+def test_smolvla_c4_small_batches(cuda, B, pick):
+    """C4 at the sweep's small batches (one-CTA GEMM tiles, 64-row A boxes at B = 1,
+    weight prefetch before the launch-overlap wait) against the oracle."""
+    from vla_b200 import device as dev
+    from vla_b200.model import SmolVLA
+    cfg = SmolVLACfg()
+    params = W.smolvla_params(cfg, seed=0)
+    obs = W.observation_batch(cfg, B, seed=3)
+    m = SmolVLA(cfg, params, "cuda")
+    out = m.infer(*(obs[k].cuda() for k in ("images", "token_ids", "state", "noise")), use_graph=True).cpu()
+    dev.sync_check()
+    sub = {k: v[pick] for k, v in obs.items()}
+    with torch.no_grad():
+        ref32 = R.smolvla_chunk(sub, params, cfg, dt=F32)
+        refbf = R.smolvla_chunk(sub, params, cfg, dt=BF)
+    for j, b in enumerate(pick):
+        check(out[b], ref32[j], refbf[j], f"C4 B={B} observation {b}")
+
+
 def test_llama_block_rope_cross(cuda):
     """The Allo cross block at the reference module's shape (SEQ 64, EMBD 768, 15/5 heads,
     FFN 3072, RoPE base 1e4): Q and the given key rotated, causal mask."""
