@@ -226,3 +226,49 @@ def test_gemm_split_k_rejects_bad_requests(cuda):
         dev.gemm(a, w, out, tile_n=32, splits=4)  # 2 k-blocks cannot feed 4 CTAs
     with pytest.raises(_lib.VlaError):
         dev.gemm(a, w, out, tile_n=96, splits=2)
+
+
+@pytest.mark.parametrize("M,N,K", [(50, 720, 2048), (64, 720, 960), (1, 736, 720), (50, 720, 256), (33, 208, 296),
+                                   (50, 96, 1000), (17, 4096, 1088), (50, 1600, 720)])
+@pytest.mark.parametrize("epi", ["plain", "bias_res", "swiglu", "rope"])
+def test_gemm_skinny(cuda, M, N, K, epi):
+    """M <= 64: four k-blocks per stage through k-slab TMA boxes (gemm_skinny.cuh),
+    with partial last units and K tails that are not whole k-blocks.  Same bits as
+    the one-k-block-per-stage kernel (tile width 96 is not a skinny width) and the
+    fp32 product within the GEMM tolerance."""
+    import torch.nn.functional as F
+    from oracle import smolvla_ref as R
+    from vla_b200 import _lib, device as dev
+    from vla_b200.model import rope_table
+    if (epi == "rope" and N % 64) or (epi == "swiglu" and N % 32):
+        pytest.skip("RoPE needs N % 64 == 0, SwiGLU N % 32 == 0")
+    g = torch.Generator().manual_seed(M * 131 + N + K)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16)
+    y = a.float() @ w.float().T
+    skinny_tile, plain_tile = (64, 192) if epi == "rope" else (32, 96)
+    if epi == "plain":
+        e, ref, cols = None, y, N
+    elif epi == "bias_res":
+        b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g).to(torch.bfloat16)
+        e, ref, cols = dev.make_epilogue(bias=b.cuda(), residual=r.cuda()), y + b.float() + r.float(), N
+    elif epi == "swiglu":
+        e, cols = dev.make_epilogue(act=_lib.ACT_SWIGLU), N // 2
+        yy = y.view(M, N // 32, 2, 16)
+        ref = (F.silu(yy[:, :, 0]) * yy[:, :, 1]).reshape(M, N // 2)
+    else:
+        cs = rope_table(50, 64, 1e4).cuda()
+        nrot = N - 64 if N > 64 else N
+        e = dev.make_epilogue(act=_lib.ACT_ROPE, rope_cs=cs, rope_seq=50, rope_ncols=nrot)
+        pos = (torch.arange(M) % 50).float()
+        rot = R.apply_rope(y[:, :nrot].reshape(M, 1, nrot // 64, 64), 1e4, positions=pos[:, None]).reshape(M, nrot)
+        ref, cols = torch.cat([rot, y[:, nrot:]], 1), N
+    outs = []
+    for tile in (skinny_tile, plain_tile):
+        out = torch.full((M, cols), float("nan"), dtype=torch.bfloat16, device="cuda")
+        dev.gemm(a.cuda(), w.cuda(), out, e, tile_n=tile)
+        outs.append(out.cpu())
+    dev.sync_check()
+    torch.testing.assert_close(outs[0].float(), ref, atol=3e-2, rtol=2e-2)
+    assert torch.equal(outs[0], outs[1]), "skinny and one-k-block-per-stage kernels differ"

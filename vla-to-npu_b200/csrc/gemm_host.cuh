@@ -4,6 +4,7 @@
 #include "gemm.cuh"
 #include "gemm2.cuh"
 #include "gemm_splitk.cuh"
+#include "gemm_skinny.cuh"
 #include "host_common.cuh"
 
 namespace vla {
@@ -155,6 +156,52 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CU
     prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 1);
   }
   return launch_status("gemm_bf16_tc");
+}
+
+// Skinny launch (M <= 64, gemm_skinny.cuh): ta is the 64-row two-dimensional
+// A map; the k-slab maps of A and B are made here.
+template <int BN>
+static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, const void* B, int64_t ldb,
+                         const CUtensorMap& tc, const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N, int64_t K,
+                         cudaStream_t st) {
+  using Cf = CfgK<BN>;
+  CUtensorMap tb, ta3, tb3;
+  int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
+  if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kSkinnyRows, kSkinnyKps);
+  if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN, kSkinnyKps);
+  if (rc) return rc;
+  static thread_local int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cf::SMEM_BYTES));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const int64_t tiles = (N + BN - 1) / BN;
+  const int sms = device_info().num_sms;
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  prof_begin(st);
+  launch_k(gemm_bf16_skinny_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
+           (int)M, (int)N, (int)K);
+  {
+    const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
+    double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
+    if (ep.residual) bytes += 2.0 * M * out_cols;
+    if (ep.act == VLA_ACT_EULER) bytes += 8.0 * M * N;
+    prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 1);
+  }
+  return launch_status("gemm_bf16_skinny");
+}
+
+// The skinny kernel serves M <= 64 with at least one whole stage of k-blocks
+// at the tile widths it is built for; VLA_GEMM_SKINNY=0 turns it off (A/B).
+static bool use_skinny(int64_t M, int64_t K, int bn) {
+  static const bool on = [] {
+    const char* v = getenv("VLA_GEMM_SKINNY");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  return on && M <= kSkinnyRows && K / BK >= kSkinnyKps && (bn == 32 || bn == 64 || bn == 128);
 }
 
 // Largest number of co-resident clusters of S split-K CTAs (kernel<BN>), cached.
@@ -416,6 +463,14 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
     rc = make_tmap_bf16_2d(&plan.ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 64);
     if (rc) return rc;
     plan.ep.a_rows = 64;
+    if (use_skinny(M, K, bn)) {
+      switch (bn) {
+        case 32: return launch_skinny<32>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        case 64: return launch_skinny<64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        case 128: return launch_skinny<128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        default: break;
+      }
+    }
   }
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);

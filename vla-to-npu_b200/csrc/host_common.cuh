@@ -99,6 +99,28 @@ static int make_tmap_bf16_2d(CUtensorMap* m, const void* ptr, uint64_t inner, ui
   return VLA_OK;
 }
 
+// K-slab view of a row-major [outer, inner] bf16 matrix: dimensions (64
+// columns, outer rows, inner / 64 whole k-blocks), strides (ld * 2 bytes, 128
+// bytes), box (64, box_outer, box_kb), 128-byte swizzle.  One box is box_kb
+// consecutive (box_outer x 128-byte) k-block tiles.  Columns past the last
+// whole k-block are not covered (the two-dimensional map serves them).
+static int make_tmap_bf16_kslab(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                                uint32_t box_outer, uint32_t box_kb) {
+  auto enc = tmap_encoder();
+  if (enc == nullptr) return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {64, outer, inner / 64};
+  cuuint64_t strides[2] = {ld * 2, 128};
+  cuuint32_t box[3] = {64, box_outer, box_kb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VLA_E_CUDA, "cuTensorMapEncodeTiled (k-slab) failed (%d): inner=%llu outer=%llu ld=%llu", (int)r,
+                     (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)ld);
+  return VLA_OK;
+}
+
 // Launch overlap (programmatic dependent launch) for every kernel of this
 // library; on by default, switchable with vla_set_launch_overlap().
 static std::atomic<int> g_launch_overlap{1};

@@ -51,6 +51,8 @@ def make_epilogue(bias=None, residual=None, res_row_mod=0, act=_lib.ACT_NONE, al
     e.ldx = 0 if euler_x is None else _rowmajor(euler_x, "euler_x")
     e.euler_dt = euler_dt
     e.b_static = 1 if b_static else 0
+    # the struct holds raw device addresses: keep the tensors alive with it
+    e._keep = (bias, residual, rope_cs, euler_x)
     return e
 
 
