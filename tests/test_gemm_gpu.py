@@ -229,10 +229,12 @@ def test_gemm_split_k_rejects_bad_requests(cuda):
 
 
 @pytest.mark.parametrize("M,N,K", [(50, 720, 2048), (64, 720, 960), (1, 736, 720), (50, 720, 256), (33, 208, 296),
-                                   (50, 96, 1000), (17, 4096, 1088), (50, 1600, 720)])
+                                   (50, 96, 1000), (17, 4096, 1088), (50, 1600, 720), (113, 960, 2560),
+                                   (100, 736, 720), (128, 1600, 960)])
 @pytest.mark.parametrize("epi", ["plain", "bias_res", "swiglu", "rope"])
 def test_gemm_skinny(cuda, M, N, K, epi):
-    """M <= 64: four k-blocks per stage through k-slab TMA boxes (gemm_skinny.cuh),
+    """One row tile (M <= 64 with 64-row copies, M <= 128 with 128-row copies):
+    four k-blocks per stage through k-slab TMA boxes (gemm_skinny.cuh),
     with partial last units and K tails that are not whole k-blocks.  Same bits as
     the one-k-block-per-stage kernel (tile width 96 is not a skinny width) and the
     fp32 product within the GEMM tolerance."""

@@ -158,23 +158,23 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CU
   return launch_status("gemm_bf16_tc");
 }
 
-// Skinny launch (M <= 64, gemm_skinny.cuh): ta is the 64-row two-dimensional
-// A map; the k-slab maps of A and B are made here.
-template <int BN>
+// Skinny launch (M <= 128, gemm_skinny.cuh): ta is the two-dimensional A map
+// with AR-row boxes; the k-slab maps of A and B are made here.
+template <int BN, int AR>
 static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, const void* B, int64_t ldb,
                          const CUtensorMap& tc, const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N, int64_t K,
                          cudaStream_t st) {
-  using Cf = CfgK<BN>;
+  using Cf = CfgK<BN, AR>;
   CUtensorMap tb, ta3, tb3;
   int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
-  if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kSkinnyRows, kSkinnyKps);
+  if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, AR, kSkinnyKps);
   if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN, kSkinnyKps);
   if (rc) return rc;
   static thread_local int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_dev_mask & (1 << (dev & 31)))) {
-    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cf::SMEM_BYTES));
     attr_dev_mask |= 1 << (dev & 31);
   }
@@ -182,7 +182,7 @@ static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, cons
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
   prof_begin(st);
-  launch_k(gemm_bf16_skinny_kernel<BN>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
+  launch_k(gemm_bf16_skinny_kernel<BN, AR>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
            (int)M, (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -194,14 +194,18 @@ static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, cons
   return launch_status("gemm_bf16_skinny");
 }
 
-// The skinny kernel serves M <= 64 with at least one whole stage of k-blocks
-// at the tile widths it is built for; VLA_GEMM_SKINNY=0 turns it off (A/B).
+// The skinny kernel serves one row tile (M <= 64 with 64-row copies at tile
+// widths 32 / 64 / 128, M <= 128 with 128-row copies at 32 / 64, where two
+// stages still fit) with at least one whole stage of k-blocks;
+// VLA_GEMM_SKINNY=0 turns it off (A/B).
 static bool use_skinny(int64_t M, int64_t K, int bn) {
   static const bool on = [] {
     const char* v = getenv("VLA_GEMM_SKINNY");
     return v == nullptr || atoi(v) != 0;
   }();
-  return on && M <= kSkinnyRows && K / BK >= kSkinnyKps && (bn == 32 || bn == 64 || bn == 128);
+  if (!on || K / BK < kSkinnyKps) return false;
+  if (M <= kSkinnyRows) return bn == 32 || bn == 64 || bn == 128;
+  return M <= BM && (bn == 32 || bn == 64);
 }
 
 // Largest number of co-resident clusters of S split-K CTAs (kernel<BN>), cached.
@@ -465,12 +469,15 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
     plan.ep.a_rows = 64;
     if (use_skinny(M, K, bn)) {
       switch (bn) {
-        case 32: return launch_skinny<32>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
-        case 64: return launch_skinny<64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
-        case 128: return launch_skinny<128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        case 32: return launch_skinny<32, 64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        case 64: return launch_skinny<64, 64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+        case 128: return launch_skinny<128, 64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
         default: break;
       }
     }
+  } else if (use_skinny(M, K, bn)) {
+    if (bn == 32) return launch_skinny<32, 128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+    if (bn == 64) return launch_skinny<64, 128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
   }
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);

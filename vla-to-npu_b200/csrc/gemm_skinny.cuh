@@ -1,5 +1,6 @@
-// One-CTA tcgen05 GEMM for skinny problems (M <= 64 rows: one observation's
-// action rows), whose time is the per-k-block cost of the main loop.
+// One-CTA tcgen05 GEMM for skinny problems (one row tile: M <= 64 rows, one
+// observation's action rows, copied as 64-row boxes; or M <= 128, its prefix
+// tokens, as 128-row boxes), whose time is the per-k-block cost of the main loop.
 //
 // Measured on B200 with the one-k-block-per-stage ring of gemm.cuh at M = 50:
 // a launch costs ~3 us plus ~530 SM cycles per 64-wide k-block whatever the
@@ -30,13 +31,13 @@
 namespace vla {
 namespace gemm {
 
-constexpr int kSkinnyRows = 64;  // A rows of every copy (M <= 64)
+constexpr int kSkinnyRows = 64;  // A rows of every copy for M <= 64; M <= 128 copies 128 rows
 constexpr int kSkinnyKps = 4;    // k-blocks per stage
 
-template <int BN>
+template <int BN, int AR>
 struct CfgK {
   static constexpr int KPS = kSkinnyKps;
-  static constexpr int A_KB = kSkinnyRows * BK * 2;  // 8 KB
+  static constexpr int A_KB = AR * BK * 2;  // 8 or 16 KB
   static constexpr int B_KB = BN * BK * 2;
   static constexpr int A_UNIT = KPS * A_KB;
   static constexpr int B_UNIT = KPS * B_KB;
@@ -59,20 +60,20 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
 
 // tmA / tmB: two-dimensional maps (64 x 64-row and 64 x BN boxes) for partial
 // units; tmA3 / tmB3: the k-slab maps (64, rows, K / 64) with (64, R, KPS) boxes.
-template <int BN>
+template <int BN, int AR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmA3, const __grid_constant__ CUtensorMap tmB3,
                             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
                             int M, int N, int K) {
-  using Cf = CfgK<BN>;
+  using Cf = CfgK<BN, AR>;
   constexpr int STAGES = Cf::STAGES;
   constexpr int KPS = Cf::KPS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // The MMA reads 128 A rows from each 64-row tile: the upper 64 come from the
-  // next tile (the last one's from the B units); those rows only produce
-  // accumulator rows >= 64 > M, which are never stored.
+  // With 64-row copies (AR = 64) the MMA reads 128 A rows from each tile: the
+  // upper 64 come from the next tile (the last one's from the B units); those
+  // rows only produce accumulator rows >= 64 > M, which are never stored.
   uint8_t* sA = base;
   uint8_t* sB = base + STAGES * Cf::A_UNIT;
   uint8_t* sC = sB + STAGES * Cf::B_UNIT;
