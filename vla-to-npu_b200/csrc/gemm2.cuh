@@ -19,17 +19,21 @@
 namespace vla {
 namespace gemm {
 
-template <int BN>
+// KPS k-blocks per stage: with KPS > 1 a stage is filled by one k-slab TMA box
+// per operand (gemm_skinny.cuh explains the per-stage costs this amortises).
+template <int BN, int KPS = 1>
 struct Cfg2 {
-  static constexpr int A_BYTES = BM * BK * 2;        // 128 rows of A per CTA
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // half of the B tile per CTA
+  static constexpr int A_KB = BM * BK * 2;           // 128 rows of A per CTA and k-block
+  static constexpr int B_KB = (BN / 2) * BK * 2;     // half of the B tile per CTA and k-block
+  static constexpr int A_BYTES = KPS * A_KB;
+  static constexpr int B_BYTES = KPS * B_KB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BUDGET = kSmemLimit - 1024 - kBarrierBytes - kEpiStoreBytes;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "UMMA N");
-  static_assert(B_BYTES % 1024 == 0, "B half-tile alignment (BN/2 multiple of 8)");
+  static_assert(B_KB % 1024 == 0, "B half-tile alignment (BN/2 multiple of 8)");
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -53,6 +57,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t bar_clust
   asm volatile("mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster_addr),
                "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int x,
+                                                 int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster_addr)
+      : "memory");
 }
 
 // Relaxed remote arrive: used only to hand a tensor-memory accumulator back to
@@ -93,13 +106,17 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
-template <int BN>
+// tmA3 / tmB3: k-slab maps (64, rows, K / 64) with (64, 128, KPS) and
+// (64, BN / 2, KPS) boxes, used when KPS > 1 for units of whole k-blocks.
+template <int BN, int KPS = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmA3, const __grid_constant__ CUtensorMap tmB3,
                          const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
                          int M, int N, int K) {
-  using Cf = Cfg2<BN>;
+  using Cf = Cfg2<BN, KPS>;
   constexpr int STAGES = Cf::STAGES;
+  static_assert(STAGES >= 2, "pair GEMM: two stages");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -122,6 +139,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
+  const int nfull = K / BK;
+  const int nunits = (num_kb + KPS - 1) / KPS;
+  auto unit_kbs = [&](int u) { return min(KPS, num_kb - u * KPS); };
+  auto unit_slab = [&](int u) { return KPS > 1 && u * KPS + KPS <= nfull; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -137,6 +158,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (KPS > 1) {
+      tma_prefetch_desc(&tmA3);
+      tma_prefetch_desc(&tmB3);
+    }
     if (ep.tma_c) tma_prefetch_desc(&tmC);
     if (ep.tma_r) tma_prefetch_desc(&tmR);
   }
@@ -160,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = cluster; t < num_tiles && ok; t += n_clusters) {
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int arow = mb * 2 * BM + (int)rank * BM, brow = nb * BN + (int)rank * (BN / 2);
+        for (int u = 0; u < nunits; ++u) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
@@ -168,9 +194,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t leader_full = map_to_rank(smem_u32(&full[s]), 0);
-          mbar_arrive_expect_tx_cluster(leader_full, Cf::STAGE_BYTES);
-          tma_load_2d_pair(sA + s * Cf::A_BYTES, &tmA, leader_full, kb * BK, mb * 2 * BM + (int)rank * BM);
-          tma_load_2d_pair(sB + s * Cf::B_BYTES, &tmB, leader_full, kb * BK, nb * BN + (int)rank * (BN / 2));
+          const int cnt = unit_kbs(u);
+          if (unit_slab(u)) {
+            mbar_arrive_expect_tx_cluster(leader_full, Cf::STAGE_BYTES);
+            tma_load_3d_pair(sA + s * Cf::A_BYTES, &tmA3, leader_full, 0, arow, u * KPS);
+            tma_load_3d_pair(sB + s * Cf::B_BYTES, &tmB3, leader_full, 0, brow, u * KPS);
+          } else {
+            mbar_arrive_expect_tx_cluster(leader_full, (uint32_t)(cnt * (Cf::A_KB + Cf::B_KB)));
+            for (int i = 0; i < cnt; ++i) {
+              const int kb = u * KPS + i;
+              tma_load_2d_pair(sA + s * Cf::A_BYTES + i * Cf::A_KB, &tmA, leader_full, kb * BK, arow);
+              tma_load_2d_pair(sB + s * Cf::B_BYTES + i * Cf::B_KB, &tmB, leader_full, kb * BK, brow);
+            }
+          }
           ++it;
         }
       }
@@ -198,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(as * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int u = 0; u < nunits; ++u) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
@@ -206,12 +242,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = make_sw128_desc(smem_u32(sA + s * Cf::A_BYTES));
-          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + s * Cf::B_BYTES));
+          const int cnt = unit_kbs(u);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc_mma_bf16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                             (kb | k) != 0 ? 1u : 0u);
+          for (int i = 0; i < KPS; ++i) {
+            if (i < cnt) {
+              const uint64_t adesc = make_sw128_desc(smem_u32(sA + s * Cf::A_BYTES + i * Cf::A_KB));
+              const uint64_t bdesc = make_sw128_desc(smem_u32(sB + s * Cf::B_BYTES + i * Cf::B_KB));
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                tc_mma_bf16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                                 (u | i | k) != 0 ? 1u : 0u);
+            }
+          }
           tc_commit_pair(&empty[s]);
           ++it;
         }

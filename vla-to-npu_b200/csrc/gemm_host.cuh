@@ -30,9 +30,9 @@ static int choose_bn(int64_t M, int64_t N, int act, int num_sms) {
   return best;
 }
 
-// Largest number of co-resident 2-CTA clusters of the pair kernel<BN> (GPC
+// Largest number of co-resident 2-CTA clusters of the pair kernel<BN, KPS> (GPC
 // boundaries can leave SMs without a partner), cached per device and width.
-template <int BN>
+template <int BN, int KPS>
 static int max_pair_clusters() {
   static int cached[64] = {};
   int dev = 0;
@@ -42,7 +42,7 @@ static int max_pair_clusters() {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Cfg2<BN>::SMEM_BYTES;
+    cfg.dynamicSmemBytes = Cfg2<BN, KPS>::SMEM_BYTES;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -51,36 +51,45 @@ static int max_pair_clusters() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc2_kernel<BN>, &cfg) != cudaSuccess || n <= 0)
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tc2_kernel<BN, KPS>, &cfg) != cudaSuccess || n <= 0)
       n = device_info().num_sms / 2;
     cached[dev] = n;
   }
   return cached[dev];
 }
 
-template <int BN>
-static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const CUtensorMap& tc, const CUtensorMap& tr,
-                      const DevEpi& ep,
-                      int64_t M, int64_t N, int64_t K, cudaStream_t st) {
-  using Cf = Cfg2<BN>;
-  CUtensorMap tb;
+template <int BN, int KPS>
+static int launch_bn2_k(const CUtensorMap& ta, const void* A, int64_t lda, const void* B, int64_t ldb,
+                        const CUtensorMap& tc, const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N,
+                        int64_t K, cudaStream_t st) {
+  using Cf = Cfg2<BN, KPS>;
+  CUtensorMap tb, ta3, tb3;
   int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN / 2);
   if (rc) return rc;
+  if (KPS > 1) {
+    rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM, KPS);
+    if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN / 2, KPS);
+    if (rc) return rc;
+  } else {
+    ta3 = ta;
+    tb3 = tb;
+  }
   static thread_local int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_dev_mask & (1 << (dev & 31)))) {
-    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN, KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cf::SMEM_BYTES));
-    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+    VLA_CUDA_TRY(
+        cudaFuncSetAttribute(gemm_bf16_tc2_kernel<BN, KPS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
     attr_dev_mask |= 1 << (dev & 31);
   }
   const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
-  const int clusters = max_pair_clusters<BN>();
+  const int clusters = max_pair_clusters<BN, KPS>();
   const int grid = 2 * (int)(tiles < clusters ? tiles : clusters);
   prof_begin(st);
-  launch_k_cluster(gemm_bf16_tc2_kernel<BN>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, tc, tr, ep, (int)M,
-                   (int)N, (int)K);
+  launch_k_cluster(gemm_bf16_tc2_kernel<BN, KPS>, 2, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3,
+                   tc, tr, ep, (int)M, (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);
@@ -89,6 +98,30 @@ static int launch_bn2(const CUtensorMap& ta, const void* B, int64_t ldb, const C
     prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 2);
   }
   return launch_status("gemm_bf16_tc2");
+}
+
+// k-blocks per stage of the pair kernel: 2 (one k-slab box per operand fills
+// a stage; measured +6 to +14 % on the 720- to 960-wide GEMMs of the step, equal
+// on the rest, and 4 no better); VLA_GEMM_PAIR_KPS=1|2|4 overrides (A/B).
+static int pair_kps(int64_t K) {
+  static const int env = [] {
+    const char* v = getenv("VLA_GEMM_PAIR_KPS");
+    const int k = v ? atoi(v) : 2;
+    return (k == 2 || k == 4) ? k : 1;
+  }();
+  return K / BK >= env ? env : 1;
+}
+
+template <int BN>
+static int launch_bn2(const CUtensorMap& ta, const void* A, int64_t lda, const void* B, int64_t ldb,
+                      const CUtensorMap& tc, const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N, int64_t K,
+                      cudaStream_t st) {
+  const int kps = pair_kps(K);
+  if constexpr (Cfg2<BN, 4>::STAGES >= 2) {
+    if (kps == 4) return launch_bn2_k<BN, 4>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+  }
+  if (kps >= 2) return launch_bn2_k<BN, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+  return launch_bn2_k<BN, 1>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
 }
 
 // One-CTA tile or CTA pair (gemm2.cuh).  The pair halves each SM's B staging
@@ -100,27 +133,26 @@ static int choose_ctas(int64_t M, int bn) {
   return (M >= 32 * BM && bn >= 64) ? 2 : 1;
 }
 
-// Tile width of a CTA-pair launch.  A k-block of the pair's main loop costs
-// about the same time for every width up to 256 (the copies' loaded latency,
-// not the 256 x BN x 64 MMA, sets its pace: measured ~555 SM cycles per k-block
-// at BN = 192 and 256), so a tile's time hardly depends on BN and the launch
-// time follows the number of waves of 256 x BN tiles over the pairs.  Take the
-// fewest waves; among equal counts the least padding past N, then the widest
-// tile (fewer tiles, fewer epilogue passes).
+// Tile width of a CTA-pair launch.  With two k-blocks per stage (pair_kps) a
+// tile's main loop costs about its width (the MMA's pace) plus a fixed share
+// (the copies' and barriers' per-stage costs, the epilogue tail); a launch
+// costs its waves of 256 x BN tiles over the pairs.  Measured at M = 12800
+// (graph-timed TFLOP/s, widths 256 / 192 / 160 / 128): N = 720 K = 960
+// 793 / 853 / 728 / 660, N = 1600 K = 720 973 / 890 / 924 / 805, which
+// waves x (BN + 96) ranks correctly; equal costs keep the wider tile.
 static int choose_bn_pair(int64_t M, int64_t N, int act, int num_sms) {
   const int cands[5] = {256, 224, 192, 160, 128};
   const int64_t pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
   int best = 0;
-  int64_t best_waves = 0, best_padded = 0;
+  int64_t best_cost = 0;
   for (int bn : cands) {
     if (act == VLA_ACT_ROPE && bn % 64 != 0) continue;
     const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + bn - 1) / bn);
     const int64_t waves = (tiles + pairs - 1) / pairs;
-    const int64_t padded = ((N + bn - 1) / bn) * bn;
-    if (best == 0 || waves < best_waves || (waves == best_waves && padded < best_padded)) {
+    const int64_t cost = waves * (bn + 96);
+    if (best == 0 || cost < best_cost) {
       best = bn;
-      best_waves = waves;
-      best_padded = padded;
+      best_cost = cost;
     }
   }
   return best;
@@ -451,13 +483,13 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   if (ctas == 2 && bn < 64) return run(A, lda, B, ldb, C, ldc, M, N, K, e, st, 64, 2);
   if (ctas == 2) {
     switch (bn) {
-      case 256: return launch_bn2<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 224: return launch_bn2<224>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 192: return launch_bn2<192>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 160: return launch_bn2<160>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 128: return launch_bn2<128>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 96: return launch_bn2<96>(ta, B, ldb, tc, tr, ep, M, N, K, st);
-      case 64: return launch_bn2<64>(ta, B, ldb, tc, tr, ep, M, N, K, st);
+      case 256: return launch_bn2<256>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 224: return launch_bn2<224>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 192: return launch_bn2<192>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 160: return launch_bn2<160>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 128: return launch_bn2<128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 96: return launch_bn2<96>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 64: return launch_bn2<64>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
       default: return set_error(VLA_E_UNSUPPORTED, "gemm: pair tile width %d not built", bn);
     }
   }
