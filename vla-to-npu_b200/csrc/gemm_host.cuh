@@ -192,29 +192,29 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, const CU
 
 // Skinny launch (M <= 128, gemm_skinny.cuh): ta is the two-dimensional A map
 // with AR-row boxes; the k-slab maps of A and B are made here.
-template <int BN, int AR>
+template <int BN, int AR, int KPS = kSkinnyKps>
 static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, const void* B, int64_t ldb,
                          const CUtensorMap& tc, const CUtensorMap& tr, const DevEpi& ep, int64_t M, int64_t N, int64_t K,
                          cudaStream_t st) {
-  using Cf = CfgK<BN, AR>;
+  using Cf = CfgK<BN, AR, KPS>;
   CUtensorMap tb, ta3, tb3;
   int rc = make_tmap_bf16_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, BN);
-  if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, AR, kSkinnyKps);
-  if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN, kSkinnyKps);
+  if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, AR, KPS);
+  if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN, KPS);
   if (rc) return rc;
   static thread_local int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_dev_mask & (1 << (dev & 31)))) {
-    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN, AR, KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cf::SMEM_BYTES));
     attr_dev_mask |= 1 << (dev & 31);
   }
-  const int64_t tiles = (N + BN - 1) / BN;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
   prof_begin(st);
-  launch_k(gemm_bf16_skinny_kernel<BN, AR>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
+  launch_k(gemm_bf16_skinny_kernel<BN, AR, KPS>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
            (int)M, (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
@@ -224,6 +224,20 @@ static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, cons
     prof_end(st, VLA_KIND_GEMM, 2.0 * M * N * K, bytes, M, N, K, BN, 1);
   }
   return launch_status("gemm_bf16_skinny");
+}
+
+// One-CTA launches of more than one row tile whose tiles fit one wave, at tile
+// widths up to 128 (three or more stages of two k-blocks), go through the unit
+// kernel (measured: B = 8 chunk 685 -> 701 chunks/s; at B = 64, where the
+// expert's 3200-row GEMMs take 256-wide tiles with two such stages, it lost
+// 1.5-3 % and is not used).  VLA_GEMM_UNIT2=0 turns it off (A/B).
+static bool use_unit2(int64_t M, int64_t N, int64_t K, int bn) {
+  static const bool on = [] {
+    const char* v = getenv("VLA_GEMM_UNIT2");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  return on && bn <= 128 && K / BK >= 2 && tiles <= device_info().num_sms;
 }
 
 // The skinny kernel serves one row tile (M <= 64 with 64-row copies at tile
@@ -510,6 +524,18 @@ static int run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, 
   } else if (use_skinny(M, K, bn)) {
     if (bn == 32) return launch_skinny<32, 128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
     if (bn == 64) return launch_skinny<64, 128>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+  } else if (use_unit2(M, N, K, bn)) {
+    switch (bn) {
+      case 256: return launch_skinny<256, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 224: return launch_skinny<224, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 192: return launch_skinny<192, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 160: return launch_skinny<160, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 128: return launch_skinny<128, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 96: return launch_skinny<96, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 64: return launch_skinny<64, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      case 32: return launch_skinny<32, 128, 2>(ta, A, lda, B, ldb, tc, tr, ep, M, N, K, st);
+      default: break;
+    }
   }
   switch (bn) {
     case 256: return launch_bn<256>(ta, B, ldb, tc, tr, ep, M, N, K, st);

@@ -34,9 +34,9 @@ namespace gemm {
 constexpr int kSkinnyRows = 64;  // A rows of every copy for M <= 64; M <= 128 copies 128 rows
 constexpr int kSkinnyKps = 4;    // k-blocks per stage
 
-template <int BN, int AR>
+template <int BN, int AR, int KPS_ = kSkinnyKps>
 struct CfgK {
-  static constexpr int KPS = kSkinnyKps;
+  static constexpr int KPS = KPS_;
   static constexpr int A_KB = AR * BK * 2;  // 8 or 16 KB
   static constexpr int B_KB = BN * BK * 2;
   static constexpr int A_UNIT = KPS * A_KB;
@@ -46,7 +46,7 @@ struct CfgK {
   static constexpr int STAGES = (BUDGET / UNIT_BYTES) > 4 ? 4 : (BUDGET / UNIT_BYTES);
   static constexpr int TMEM_COLS = Cfg<BN>::TMEM_COLS;
   static constexpr int SMEM_BYTES = STAGES * UNIT_BYTES + kEpiStoreBytes + kBarrierBytes + 1024;
-  static_assert(STAGES >= 2, "skinny GEMM: two stages of four k-blocks must fit");
+
   static_assert(A_UNIT % 1024 == 0 && B_UNIT % 1024 == 0, "unit alignment");
 };
 
@@ -60,14 +60,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
 
 // tmA / tmB: two-dimensional maps (64 x 64-row and 64 x BN boxes) for partial
 // units; tmA3 / tmB3: the k-slab maps (64, rows, K / 64) with (64, R, KPS) boxes.
-template <int BN, int AR>
+template <int BN, int AR, int KPS_ = kSkinnyKps>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmA3, const __grid_constant__ CUtensorMap tmB3,
                             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
                             int M, int N, int K) {
-  using Cf = CfgK<BN, AR>;
+  using Cf = CfgK<BN, AR, KPS_>;
   constexpr int STAGES = Cf::STAGES;
+  static_assert(STAGES >= 2, "unit GEMM: two stages must fit");
   constexpr int KPS = Cf::KPS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
