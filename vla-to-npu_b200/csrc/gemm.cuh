@@ -464,8 +464,10 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
         prefetch32(ep, m, n + step, row_ok, nxt);
         if (ep.tma_r) res_load(tmR, es, es.sb ^ 1, n + step, rrow, 0, lane);
       }
+      if (ep.alpha != 1.f) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
+        for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
+      }
       finish32(ep, m, n, orow, v, row_ok, cur, tmC, es, lane);
       if (more) cur = nxt;
     }
