@@ -331,10 +331,12 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
       ps.add16(64 * h + 16 * hq, lo);
       ps.add16(64 * h + 32 + 16 * hq, hi);
       if (!row_ok && !ep.tma_c) continue;
+      if (ep.alpha != 1.f) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        lo[i] *= ep.alpha;
-        hi[i] *= ep.alpha;
+        for (int i = 0; i < 16; ++i) {
+          lo[i] *= ep.alpha;
+          hi[i] *= ep.alpha;
+        }
       }
       if (ep.bias != nullptr) {  // the same address on every lane: one broadcast load
         float b[8];
@@ -417,8 +419,13 @@ __device__ __forceinline__ void epilogue_tile(const DevEpi& ep, uint32_t taddr, 
       const int n = n0 + c;
       if (n >= ep.N) break;
       if (!row_ok && !ep.tma_c) continue;
+      if (ep.alpha != 1.f) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * ep.alpha) * (u[i] * ep.alpha);
+        for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i] * ep.alpha) * (u[i] * ep.alpha);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[i] = silu_f(g[i]) * u[i];
+      }
       const int nc = n >> 1;
       if (ep.residual != nullptr && row_ok) {
         const uint4* rp = reinterpret_cast<const uint4*>(ep.residual + res_row(ep, m) * ep.ldr + nc);
