@@ -311,9 +311,9 @@ __device__ __forceinline__ float tanh_fast(float x) {
 __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float k0 = 0.7978845608028654f;
   const float k1 = 0.044715f;
-  const float u = x * fmaf(k0 * k1, x * x, k0);  // k0 x (1 + k1 x^2)
+  const float u = k0 * x * (1.f + k1 * x * x);
   const float hx = 0.5f * x;
-  return fmaf(hx, tanh_fast(u), hx);
+  return hx + hx * tanh_fast(u);
 }
 
 // SiLU x * sigmoid(x), with sigmoid(x) = 0.5 + 0.5 tanh(x / 2).
