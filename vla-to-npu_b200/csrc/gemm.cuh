@@ -126,6 +126,34 @@ __device__ __forceinline__ void stage_store(const CUtensorMap* tm, EpiStore& es,
   es.sb ^= 1;
 }
 
+// RoPE's two 16-column pieces of one head (v0: columns col0.., v1: col1..),
+// staged in the warp's two buffers and stored as one bulk group: one wait, one
+// proxy fence and one commit per pair instead of per piece.
+__device__ __forceinline__ void stage_store_pair16(const CUtensorMap* tm, EpiStore& es, const uint4* v0, const uint4* v1,
+                                                   int lane, int col0, int col1) {
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int phys = i ^ ((lane >> 2) & 1);
+    st_shared_v4(es.buf + (uint32_t)(lane * 32 + phys * 16), v0[i]);
+    st_shared_v4(es.buf + (uint32_t)kStageC + (uint32_t)(lane * 32 + phys * 16), v1[i]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(es.buf), "r"(col0), "r"(es.row0)
+                 : "memory");
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(es.buf + (uint32_t)kStageC), "r"(col1), "r"(es.row0)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+
 // Stage-and-store with the residual already in the staging buffer: this lane's
 // row is read from shared memory, added to v, and the sum stored in place.
 __device__ __forceinline__ void res_stage_store(const CUtensorMap* tmC, EpiStore& es, float* v, int lane, int col) {
@@ -372,8 +400,7 @@ __device__ __forceinline__ void rope_tile(const DevEpi& ep, uint32_t taddr, int 
       if (ep.tma_c) {  // (no residual: the host sends RoPE + residual down the direct path)
         const uint4 plo[2] = {pack_bf16x8(lo), pack_bf16x8(lo + 8)};
         const uint4 phi[2] = {pack_bf16x8(hi), pack_bf16x8(hi + 8)};
-        stage_store<2>(tmC, es, plo, lane, n + 16 * hq);
-        stage_store<2>(tmC, es, phi, lane, n + 32 + 16 * hq);
+        stage_store_pair16(tmC, es, plo, phi, lane, n + 16 * hq, n + 32 + 16 * hq);
         continue;
       }
       if (ep.residual != nullptr) {
