@@ -240,9 +240,16 @@ static int attention(const attn::Params& p, int batch, cudaStream_t st, int impl
   if (impl == VLA_ATTN_TCGEN05_SHORT) return attention_short(p, batch, st);
   // short sequences (text prefix, action expert): the pipelined kernel, 30-45 %
   // faster than the one-chain-per-CTA kernels on all three shapes
-  if (impl == VLA_ATTN_TCGEN05_PIPE || (impl == VLA_ATTN_AUTO && pipe_fits(p, batch)))
+  // With few items (batch x kv heads at most half the SMs: one or a few
+  // observations) the per-item chain (copy, S, softmax, P.V, store) of the
+  // pipelined kernel is the launch's latency, and the mma.sync kernel, whose CTAs
+  // each take one 64-query tile of one head, finishes sooner (graph-timed, 15 / 5
+  // heads: B = 1 expert self 5.0 -> 2.8 us, cross 6.1 -> 3.7, text 8.6 -> 4.1;
+  // B = 8 5.2 -> 4.3, 6.3 -> 6.2, 8.9 -> 7.5).
+  const bool few_items = (long long)batch * p.Hkv * 2 <= device_info().num_sms;
+  if (impl == VLA_ATTN_TCGEN05_PIPE || (impl == VLA_ATTN_AUTO && !few_items && pipe_fits(p, batch)))
     return attention_pipe(p, batch, st);
-  if (impl == VLA_ATTN_AUTO && p.Lk <= 128) {
+  if (impl == VLA_ATTN_AUTO && !few_items && p.Lk <= 128) {
     const long long g_rows = (long long)(p.Hq / p.Hkv) * p.Lq;
     const long long pad_short = ((g_rows + 127) / 128) * 128;
     const long long pad_mma = (long long)(p.Hq / p.Hkv) * (((long long)p.Lq + 63) / 64) * 64;
