@@ -21,10 +21,12 @@ constexpr int kMaxVec = 4;  // rows up to 32 lanes x 4 x 8 = 1024 elements stay 
 // Normalise one row whose 16-byte vectors stay in registers as packed bf16
 // (N <= 1024; 4 registers per 8 values keep the kernel at ~46 registers, so
 // more warps are resident to cover the load latency).
+// gp / bp: the lane's gain / bias vectors already in registers (or null).
 template <int MODE, int R>
 __device__ __forceinline__ void norm_rows_reg(const bf16* __restrict__ x, long long ldx, const bf16* __restrict__ g,
                                               const bf16* __restrict__ b, bf16* __restrict__ y, long long ldy,
-                                              long long row0, int M, int N, float eps, int lane) {
+                                              long long row0, int M, int N, float eps, int lane,
+                                              const uint4* gp = nullptr, const uint4* bp = nullptr) {
   const int nvec = N >> 3;
   const float inv_n = 1.f / (float)N;
   uint4 raw[R][kMaxVec];  // rows kept as packed bf16 (4 registers per 8 values)
@@ -81,8 +83,8 @@ __device__ __forceinline__ void norm_rows_reg(const bf16* __restrict__ x, long l
     const int c = lane + 32 * i;
     if (c < nvec) {
       float gg[8], bb[8];
-      unpack_bf16x8(__ldg(gv + c), gg);
-      if (MODE == 1) unpack_bf16x8(__ldg(bv + c), bb);
+      unpack_bf16x8(gp != nullptr ? gp[i] : __ldg(gv + c), gg);
+      if (MODE == 1) unpack_bf16x8(bp != nullptr ? bp[i] : __ldg(bv + c), bb);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const long long row = row0 + r;
@@ -155,17 +157,33 @@ __device__ __forceinline__ void norm_row_wide(const bf16* __restrict__ x, long l
 }
 
 // MODE 0 = RMSNorm, 1 = LayerNorm; one warp per row, the grid striding over
-// the rows.
-template <int MODE>
+// the rows.  STATIC: g and b are weights no earlier kernel in the stream
+// writes, so rows of at most 1024 take them into registers before waiting for
+// the previous kernel (their load latency overlaps its tail).
+template <int MODE, bool STATIC>
 __global__ void __launch_bounds__(kWarps * 32) rownorm_kernel(const bf16* __restrict__ x, long long ldx,
                                                               const bf16* __restrict__ g, const bf16* __restrict__ b,
                                                               bf16* __restrict__ y, long long ldy, int M, int N,
                                                               float eps) {
-  pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool reg_rows = (N >> 3) <= 32 * kMaxVec;
+  uint4 gp[kMaxVec], bp[kMaxVec];
+  if (STATIC && reg_rows) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = lane + 32 * i;
+      gp[i] = c < (N >> 3) ? __ldg(reinterpret_cast<const uint4*>(g) + c) : make_uint4(0u, 0u, 0u, 0u);
+      bp[i] = (MODE == 1 && c < (N >> 3)) ? __ldg(reinterpret_cast<const uint4*>(b) + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  } else {
+    pdl_prologue();
+  }
   for (long long row = (long long)blockIdx.x * kWarps + warp; row < M; row += (long long)gridDim.x * kWarps) {
-    if ((N >> 3) <= 32 * kMaxVec)
-      norm_rows_reg<MODE, 1>(x, ldx, g, b, y, ldy, row, M, N, eps, lane);
+    if (reg_rows)
+      norm_rows_reg<MODE, 1>(x, ldx, g, b, y, ldy, row, M, N, eps, lane, STATIC ? gp : nullptr,
+                             STATIC ? bp : nullptr);
     else
       norm_row_wide<MODE>(x, ldx, g, b, y, ldy, row, N, eps, lane);
   }
