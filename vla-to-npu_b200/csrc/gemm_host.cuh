@@ -126,11 +126,12 @@ static int launch_bn2(const CUtensorMap& ta, const void* A, int64_t lda, const v
 
 // One-CTA tile or CTA pair (gemm2.cuh).  The pair halves each SM's B staging
 // traffic and doubles the MMA's M; inside the full C4 step (B = 256) it measured
-// faster on B200 for every GEMM shape of the step (+3-25 % per shape).  Small M
-// (below 4096 rows, e.g. the single-observation blocks, where the pair lost
-// 3-10 %) stays on one CTA per tile.
+// faster on B200 for every GEMM shape of the step (+3-25 % per shape).  With two
+// k-blocks per pair stage it also wins on the expert's 3200-row GEMMs of the
+// B = 64 step (chunk +1.5 %); small M (the single-observation blocks, below 2048
+// rows) stays on one CTA per tile.
 static int choose_ctas(int64_t M, int bn) {
-  return (M >= 32 * BM && bn >= 64) ? 2 : 1;
+  return (M >= 16 * BM && bn >= 64) ? 2 : 1;
 }
 
 // Tile width of a CTA-pair launch.  With two k-blocks per stage (pair_kps) a
