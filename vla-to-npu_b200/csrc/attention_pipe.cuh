@@ -12,10 +12,11 @@
 // One persistent CTA per SM, warp-specialised, every hand-off an mbarrier:
 //   warp 0  TMA producer: item k into smem stage k % stages (2-4 stages);
 //   warp 1  MMA issuer (one thread): per M-tile u, S = Q K^T (128 x NK x 64)
-//           into TMEM slot u % 4 (128 columns each), two tiles ahead of
-//           O = P V (A = P from TMEM, V MN-major from smem) into the slot's
-//           columns 64..127;
-//   warps 4-11  two softmax warpgroups taking alternate M-tiles: thread r owns
+//           into TMEM slot u % 4 (128 columns each), ahead of O = P V (A = P
+//           from TMEM, V MN-major from smem) into the slot's columns 64..127;
+//   warps 4..  NG softmax warpgroups (NG = 4, or 2) taking M-tiles in turn
+//           (group g: tiles g, g + NG, ..., so with 4 groups two of them share
+//           the full first tiles of 150-row items): thread r owns
 //           row r, reads S, masks keys past kv_len / above the causal diagonal,
 //           writes P = 2^(s * scale - m) as bf16 pairs over the S columns it
 //           has read, keeps the fp32 row sum; then reads O, divides, and writes
@@ -38,7 +39,9 @@ namespace attn_pipe {
 
 constexpr int HD = 64;
 constexpr int MT = 128;
-constexpr int kThreads = 384;
+// threads of a CTA with NG softmax warpgroups (warps 0-3: producer, MMA
+// issuer, store, idle)
+__host__ __device__ constexpr int threads_for(int NG) { return 128 + 128 * NG; }
 constexpr int kSlots = 4;
 constexpr uint32_t SLOT_COLS = 128;
 constexpr uint32_t O_OFF = 64;
@@ -87,8 +90,19 @@ __device__ __forceinline__ void fail(volatile int* abort_flag) {
   vla_record_error(VLA_DERR_ATTN_TIMEOUT);
 }
 
-template <int NK>
-__global__ void __launch_bounds__(kThreads, 1)
+// 32 lanes x 16 consecutive 32-bit TMEM columns from registers, then wait
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+template <int NK, int NG>
+__global__ void __launch_bounds__(threads_for(NG), 1)
     attn_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -238,12 +252,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ---------------- softmax + output rows ----------------
-    const int wg = (warp - 4) >> 2, quarter = warp & 3;
+    const int wg = (warp - 4) >> 2, quarter = warp & 3;  // M-tiles u = wg, wg + NG, ...
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int R = p.G * p.Lq;
     bool ok = true;
-    for (int u = wg; u < my_tiles; u += 2) {
+    for (int u = wg; u < my_tiles; u += NG) {
       const int k = u / p.T, t = u % p.T, s = k % p.stages;
       const int it = (int)blockIdx.x + k * (int)gridDim.x;
       const int b = it / p.Hkv;
@@ -271,23 +285,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (32 * h + c < kend) m = fmaxf(m, v[c]);
         }
         const float mb = m == -INFINITY ? 0.f : m * p.scale_log2;
+        // P of keys 32h..32h+31 goes to columns 16h..16h+15, all of them read
+        // already (this chunk's own load included)
 #pragma unroll
-        for (int h = 0; h < NK / 64; ++h) {
-          uint32_t pk[32];
+        for (int h = 0; h < NK / 32; ++h) {
+          uint32_t pk[16];
+          float v[32];
+          tmem_ld32(sc + 32 * h, v);
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            float v[32];
-            tmem_ld32(sc + 64 * h + 32 * half, v);
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              const int key = 64 * h + 32 * half + c;
-              const float e0 = key < kend ? attn_sq::ex2f(fmaf(v[c], p.scale_log2, -mb)) : 0.f;
-              const float e1 = key + 1 < kend ? attn_sq::ex2f(fmaf(v[c + 1], p.scale_log2, -mb)) : 0.f;
-              l += e0 + e1;
-              pk[16 * half + (c >> 1)] = pack_bf16x2(e0, e1);
-            }
+          for (int c = 0; c < 32; c += 2) {
+            const int key = 32 * h + c;
+            const float e0 = key < kend ? attn_sq::ex2f(fmaf(v[c], p.scale_log2, -mb)) : 0.f;
+            const float e1 = key + 1 < kend ? attn_sq::ex2f(fmaf(v[c + 1], p.scale_log2, -mb)) : 0.f;
+            l += e0 + e1;
+            pk[c >> 1] = pack_bf16x2(e0, e1);
           }
-          attn_sq::tmem_st32u(sc + 32 * h, pk);  // P over S columns already read
+          tmem_st16u(sc + 16 * h, pk);
         }
       }
       tc_fence_before();
@@ -295,24 +308,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bb.o_full[slot], par, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      // O in two 32-column halves (register pressure); the output row replaces
-      // query row srow of the item's Q tile (S of this tile has completed), in
-      // the tile's 128-byte swizzle
+      // O in 32-column halves (16-column pieces with four softmax groups, for
+      // their 96-register budget); the output row replaces query row srow of
+      // the item's Q tile (S of this tile has completed), in the tile's
+      // 128-byte swizzle
+      constexpr int OC = NG == 4 ? 16 : 32;
       const bool store_row = live && srow < R;
       const uint32_t row_addr = stage0 + (uint32_t)s * p.stage_bytes + (uint32_t)srow * 128u;
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float o[32];
-        if (live) tmem_ld32(sc + O_OFF + 32u * half, o);
-        if (half == 1) {
+      for (int piece = 0; piece < HD / OC; ++piece) {
+        float o[OC];
+        if (live) {
+          if constexpr (OC == 16)
+            tmem_ld16(sc + O_OFF + (uint32_t)(OC * piece), o);
+          else
+            tmem_ld32(sc + O_OFF + (uint32_t)(OC * piece), o);
+        }
+        if (piece == HD / OC - 1) {
           tc_fence_before();
           mbar_arrive(&bb.slot_free[slot]);
         }
         if (store_row) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c8 = 4 * half + j;
+          for (int j = 0; j < OC / 8; ++j) {
+            const int c8 = (OC / 8) * piece + j;
             float t8[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) t8[i] = o[8 * j + i] * inv;

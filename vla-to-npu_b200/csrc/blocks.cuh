@@ -206,11 +206,18 @@ static int attention_pipe(const attn::Params& p, int batch, cudaStream_t st) {
   if (!rc) rc = make_tmap_heads_4d(&tv, p.v, p.Hkv, p.Lk, batch, p.v_row, p.v_batch, 1, NK);
   if (!rc) rc = make_tmap_heads_4d(&to, p.o, p.Hq, p.Lq, batch, p.o_row, p.o_batch, G, p.Lq);
   if (rc) return rc;
-  auto kern = NK == 64 ? attn_pipe::attn_pipe_kernel<64> : attn_pipe::attn_pipe_kernel<128>;
-  static thread_local int attr_smem[2][32] = {};
+  // softmax warpgroups: 4 (two of them share the full M-tiles of a
+  // 150-row item) unless VLA_ATTN_PIPE_GROUPS=2
+  static const int groups = [] {
+    const char* v = getenv("VLA_ATTN_PIPE_GROUPS");
+    return (v != nullptr && atoi(v) == 2) ? 2 : 4;
+  }();
+  auto kern = NK == 64 ? (groups == 4 ? attn_pipe::attn_pipe_kernel<64, 4> : attn_pipe::attn_pipe_kernel<64, 2>)
+                       : (groups == 4 ? attn_pipe::attn_pipe_kernel<128, 4> : attn_pipe::attn_pipe_kernel<128, 2>);
+  static thread_local int attr_smem[2][2][32] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  int& cur = attr_smem[NK == 64][dev & 31];
+  int& cur = attr_smem[groups == 4][NK == 64][dev & 31];
   if (cur < smem) {
     VLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cur = smem;
@@ -219,7 +226,7 @@ static int attention_pipe(const attn::Params& p, int batch, cudaStream_t st) {
   const int sms = device_info().num_sms;
   const int grid = (int)(items < sms ? items : sms);
   prof_begin(st);
-  launch_k(kern, dim3(grid), dim3(attn_pipe::kThreads), smem, st, tq, tk, tv, to, pp);
+  launch_k(kern, dim3(grid), dim3(attn_pipe::threads_for(groups)), smem, st, tq, tk, tv, to, pp);
   prof_end(st, VLA_KIND_ATTENTION, 4.0 * batch * p.Hq * (double)p.Lq * p.Lk * 64,
            2.0 * batch * ((double)p.Lq * p.Hq * 64 * 2 + (double)p.Lk * p.Hkv * 64 * 2));
   return launch_status("attn_pipe");
