@@ -99,6 +99,13 @@ int vla_peek_device_error(unsigned int* code);
  * vla_sync_check() then reports VLA_E_DEVICE_TIMEOUT.  No counterpart in the
  * reference (its NPU calls have no error channel). */
 int vla_test_expired_wait(int32_t limit_us, vla_stream_t stream);
+/* Evaluates y[i] = 2^x[i] (n fp32 device values) with the FMA-pipe
+ * exponential that the SigLIP attention kernel uses for a quarter of its
+ * softmax keys (Cody-Waite split, cubic minimax fit of 2^f on [0, 1)), so its
+ * error bound can be tested against exact powers of two.  Inputs below -126
+ * give values below 2^-126.  No counterpart in the reference (its AIE softmax
+ * takes exp from a lookup table). */
+int vla_test_exp2_fma(const float* x, float* y, int64_t n, vla_stream_t stream);
 /* sizeof of the ABI structs, in the order vla_epilogue, vla_attention_args,
  * vla_llama_layer, vla_vision_layer, vla_profile_record, written to out[0..n);
  * returns the count. */

@@ -373,3 +373,27 @@ def test_camera_preprocess(cuda, B, H, W, S):
     dev.patch_im2col(img, p, ref_patches)
     dev.sync_check()
     assert torch.equal(patches, ref_patches), "fused im2col differs from resize + im2col"
+
+
+def test_exp2_fma_error_bound(cuda):
+    """The FMA-pipe exponential of the SigLIP attention softmax: relative error
+    under 1e-4 against exact 2^x over the softmax's argument range (the kernel
+    feeds x = s * scale - running max, at most +8 with the lazy rescale), values
+    below 2^-126 (no NaN, no wrap-around) for x below -126 and for -inf."""
+    import ctypes
+    from vla_b200 import _lib
+    lib = _lib.load()
+    x = torch.cat([torch.linspace(-125.0, 8.0, 1 << 20, dtype=torch.float64),
+                   torch.tensor([0.0, -0.0, 1.0, -1.0, 7.999, -1e-7, 1e-7], dtype=torch.float64)]).float().cuda()
+    y = torch.empty_like(x)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.vla_test_exp2_fma(x.data_ptr(), y.data_ptr(), x.numel(), stream))
+    torch.cuda.synchronize()
+    exact = torch.exp2(x.double())
+    rel = ((y.double() - exact) / exact).abs()
+    assert rel.max().item() < 1e-4, rel.max().item()
+    low = torch.tensor([-126.0, -126.5, -127.0, -200.0, -1e30, float("-inf")], device="cuda")
+    yl = torch.empty_like(low)
+    _lib.check(lib.vla_test_exp2_fma(low.data_ptr(), yl.data_ptr(), low.numel(), stream))
+    torch.cuda.synchronize()
+    assert torch.isfinite(yl).all() and (yl >= 0).all() and (yl < 2.0 ** -125).all(), yl.tolist()

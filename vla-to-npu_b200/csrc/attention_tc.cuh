@@ -112,6 +112,42 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float e0, float e1) {
       : "f"(e0), "f"(e1));
 }
 
+// 2^x of a pair on the FMA pipe (packed fp32 pairs), for part of the keys:
+// MUFU.EX2 serves 16 lanes per clock per SM, the FMA pipe 128, and the exp
+// phase leaves issue slots free.  Method (Cody-Waite split plus polynomial):
+// x is clamped to >= -126 (the cubic is just below 1 at f = 0, so its
+// exponent field is 126 there and n = -126 keeps the sum >= 0); r = x + 1.5 * 2^23 rounded toward -inf holds
+// n = floor(x) in its low mantissa bits, f = x - n lies in [0, 1), 2^f comes
+// from the cubic minimax fit (in relative error) of 2^f on [0, 1]
+// (0.99992514 + 0.695834 f + 0.22606707 f^2 + 0.07802403 f^3, max relative
+// error 7.5e-5, well under the 2^-9 rounding of the bf16 P it feeds), and
+// 2^n is added into the exponent field: bits(r) << 23 equals n << 23 modulo
+// 2^32 because the low nine bits of bits(1.5 * 2^23) are zero.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& e0, float& e1) {
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  uint32_t r0, r1, p0, p1;
+  asm("{\n\t.reg .b64 x, c, r, t, f, p, k;\n\t"
+      "mov.b64 x, {%4, %5};\n\t"
+      "mov.b64 c, {%6, %6};\n\t"
+      "add.rm.f32x2 r, x, c;\n\t"
+      "sub.rn.f32x2 t, r, c;\n\t"
+      "sub.rn.f32x2 f, x, t;\n\t"
+      "mov.b64 p, {%7, %7};\n\t"
+      "mov.b64 k, {%8, %8};\n\t"
+      "fma.rn.f32x2 p, p, f, k;\n\t"
+      "mov.b64 k, {%9, %9};\n\t"
+      "fma.rn.f32x2 p, p, f, k;\n\t"
+      "mov.b64 k, {%10, %10};\n\t"
+      "fma.rn.f32x2 p, p, f, k;\n\t"
+      "mov.b64 {%0, %1}, r;\n\t"
+      "mov.b64 {%2, %3}, p;\n\t}"
+      : "=r"(r0), "=r"(r1), "=r"(p0), "=r"(p1)
+      : "f"(x0), "f"(x1), "f"(12582912.f), "f"(0.07802403f), "f"(0.22606707f), "f"(0.695834f), "f"(0.99992514f));
+  e0 = __uint_as_float(r0 * 8388608u + p0);
+  e1 = __uint_as_float(r1 * 8388608u + p1);
+}
+
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -226,6 +262,9 @@ __device__ __forceinline__ int item_keys(const Params& p, int b) {
 // Persistent kernel: CTA i processes work items i, i + gridDim.x, ...  Every
 // pipeline counter (K/V ring slots, S/P/PV buffers) runs over the CTA's global
 // tile index, so loads and MMAs of the next item overlap the tail of this one.
+// P8 of every 8 key pairs take their exponentials from ex2_poly2 (FMA pipe),
+// the rest from MUFU.EX2.
+template <int P8>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, Params p) {
@@ -495,8 +534,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BKV; c += 2) {
           float x0, x1;
           fma2(sr[c], sr[c + 1], p.scale_log2, -mbase, x0, x1);
-          const float e0 = ex2_fast(x0);
-          const float e1 = ex2_fast(x1);
+          float e0, e1;
+          if (P8 > 0 && ((c >> 1) & 7) < P8) {
+            ex2_poly2(x0, x1, e0, e1);
+          } else {
+            e0 = ex2_fast(x0);
+            e1 = ex2_fast(x1);
+          }
           if (c < 8) {
             rs8[c & 7] = e0;
             rs8[(c + 1) & 7] = e1;

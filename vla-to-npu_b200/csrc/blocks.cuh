@@ -86,14 +86,22 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
   tp.kv_len = p.kv_len;
   tp.scale_log2 = p.scale_log2;
   const int smem = (int)sizeof(attn_tc::Smem) + 1024;
+  // key pairs (of every 8) whose exponentials run on the FMA pipe:
+  // VLA_ATTN_POLY8 = 0, 2 or 3
+  static const int poly8 = [] {
+    const char* v = getenv("VLA_ATTN_POLY8");
+    const int n = v != nullptr ? atoi(v) : 2;
+    return n == 0 || n == 3 ? n : 2;
+  }();
+  auto kern = poly8 == 0 ? attn_tc::flash_attn_tc_kernel<0>
+                         : (poly8 == 3 ? attn_tc::flash_attn_tc_kernel<3> : attn_tc::flash_attn_tc_kernel<2>);
   static thread_local int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_dev_mask & (1 << (dev & 31)))) {
-    VLA_CUDA_TRY(
-        cudaFuncSetAttribute(attn_tc::flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    VLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaFuncAttributes fa{};
-    VLA_CUDA_TRY(cudaFuncGetAttributes(&fa, attn_tc::flash_attn_tc_kernel));
+    VLA_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
     // the in-kernel register split (setmaxnreg) hands out exactly the launch's
     // registers: it is only sound at the register count it was sized for
     if (fa.numRegs != attn_tc::kLaunchRegs || fa.maxThreadsPerBlock < attn_tc::kThreads)
@@ -108,7 +116,7 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
   const int sms = device_info().num_sms;
   const int grid = (int)(items < sms ? items : sms);
   prof_begin(st);
-  launch_k(attn_tc::flash_attn_tc_kernel, dim3(grid), dim3(attn_tc::kThreads), smem, st, tq, tk, tv, tp);
+  launch_k(kern, dim3(grid), dim3(attn_tc::kThreads), smem, st, tq, tk, tv, tp);
   prof_end(st, VLA_KIND_ATTENTION, 4.0 * batch * p.Hq * (double)p.Lq * p.Lk * 64,
            2.0 * batch * ((double)p.Lq * p.Hq * 64 * 2 + (double)p.Lk * p.Hkv * 64 * 2));
   return launch_status("flash_attn_tc");

@@ -51,6 +51,18 @@ __global__ void expired_wait_kernel(uint64_t limit_ns) {
   if (!mbar_wait_bounded(&bar, 0u, nullptr, limit_ns)) vla_record_error(VLA_DERR_TEST_TIMEOUT);
 }
 
+// y = 2^x by the FMA-pipe exponential of the SigLIP attention's softmax
+// (attn_tc::ex2_poly2), one pair of elements per thread.
+__global__ void exp2_fma_kernel(const float* x, float* y, long long n) {
+  const long long i = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float x1 = i + 1 < n ? x[i + 1] : 0.f;
+  float e0, e1;
+  attn_tc::ex2_poly2(x[i], x1, e0, e1);
+  y[i] = e0;
+  if (i + 1 < n) y[i + 1] = e1;
+}
+
 extern "C" {
 
 const char* vla_last_error(void) { return t_last_error; }
@@ -59,6 +71,15 @@ int vla_test_expired_wait(int32_t limit_us, vla_stream_t stream) {
   VLA_CHECK_ARG(limit_us >= 1 && limit_us <= 1000000, "test_expired_wait: limit_us must be in [1, 1e6]");
   expired_wait_kernel<<<1, 32, 0, as_stream(stream)>>>((uint64_t)limit_us * 1000ull);
   return launch_status("test_expired_wait");
+}
+
+int vla_test_exp2_fma(const float* x, float* y, int64_t n, vla_stream_t stream) {
+  VLA_CHECK_ARG(x != nullptr && y != nullptr, "test_exp2_fma: null pointer");
+  VLA_CHECK_ARG(n >= 0 && n <= (1ll << 30), "test_exp2_fma: n must be in [0, 2^30]");
+  if (n == 0) return VLA_OK;
+  const long long pairs = (n + 1) / 2;
+  exp2_fma_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, as_stream(stream)>>>(x, y, n);
+  return launch_status("test_exp2_fma");
 }
 
 int vla_version(void) { return 100; }

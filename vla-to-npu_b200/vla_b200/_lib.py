@@ -124,6 +124,7 @@ SIGNATURES = {
     "vla_sync_check": [],
     "vla_peek_device_error": [ctypes.POINTER(ctypes.c_uint)],
     "vla_test_expired_wait": [_I32, _P],
+    "vla_test_exp2_fma": [_P, _P, _I64, _P],
     "vla_abi_sizes": [ctypes.POINTER(ctypes.c_int64), _I32],
     "vla_launch_count": [],
     "vla_set_launch_overlap": [_I32],
