@@ -82,6 +82,7 @@ KERNEL_CASES = {
     "attn_vision": "SigLIP non-causal attention, 16 x 12 heads x 1024 x 1024",
     "attn_text": "text-prefix causal GQA attention (short-sequence tcgen05 kernel), 256 x 15 q / 5 kv heads x 113 x 113",
     "layer_norm": "SigLIP LayerNorm, 16384 x 768",
+    "layer_norm_full": "SigLIP LayerNorm at the B = 256 step's shape, 262144 x 768 (805 MB moved, larger than L2)",
     "rms_norm": "text-width RMSNorm, 131072 x 960 (250 MB in, larger than L2)",
     "attn_exp_self": "action-expert causal self-attention, 512 x 15 q / 5 kv heads x 50 x 50 (AUTO kernel choice)",
     "attn_exp_cross": "action-expert cross-attention to the prefix, 512 x 15 q / 5 kv heads x 50 x 113 (AUTO)",
@@ -175,11 +176,12 @@ def run_kernel_case(args):
         fn = lambda: dev.rms_norm(x, g, 1e-5, out=y)  # noqa: E731
         flops, nbytes = 0.0, 4.0 * 131072 * 960
     else:
-        x = W.randn((16384, 768), 0, "kc.x").cuda()
+        rows = 262144 if name == "layer_norm_full" else 16384
+        x = W.randn((rows, 768), 0, "kc.x").cuda()
         g, bb = torch.ones(768, dtype=bf, device="cuda"), torch.zeros(768, dtype=bf, device="cuda")
         y = torch.empty_like(x)
         fn = lambda: dev.layer_norm(x, g, bb, 1e-6, out=y)  # noqa: E731
-        flops, nbytes = 0.0, 4.0 * 16384 * 768
+        flops, nbytes = 0.0, 4.0 * rows * 768
     for _ in range(max(args.warmup, 1)):
         fn()
     torch.cuda.synchronize()
