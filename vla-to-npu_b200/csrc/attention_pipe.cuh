@@ -11,9 +11,10 @@
 //
 // One persistent CTA per SM, warp-specialised, every hand-off an mbarrier:
 //   warp 0  TMA producer: item k into smem stage k % stages (2-4 stages);
-//   warp 1  MMA issuer (one thread): per M-tile u, S = Q K^T (128 x NK x 64)
-//           into TMEM slot u % 4 (128 columns each), ahead of O = P V (A = P
-//           from TMEM, V MN-major from smem) into the slot's columns 64..127;
+//   warp 1  S issuer (one thread): per M-tile u, S = Q K^T (128 x NK x 64)
+//           into TMEM slot u % 4 (128 columns each);
+//   warp 3  P.V issuer (one thread): O = P V (A = P from TMEM, V MN-major
+//           from smem) into the slot's columns 64..127 once P is written;
 //   warps 4..  NG softmax warpgroups (NG = 4, or 2) taking M-tiles in turn
 //           (group g: tiles g, g + NG, ..., so with 4 groups two of them share
 //           the full first tiles of 150-row items): thread r owns
@@ -39,8 +40,8 @@ namespace attn_pipe {
 
 constexpr int HD = 64;
 constexpr int MT = 128;
-// threads of a CTA with NG softmax warpgroups (warps 0-3: producer, MMA
-// issuer, store, idle)
+// threads of a CTA with NG softmax warpgroups (warps 0-3: producer, S issuer,
+// store, P.V issuer)
 __host__ __device__ constexpr int threads_for(int NG) { return 128 + 128 * NG; }
 constexpr int kSlots = 4;
 constexpr uint32_t SLOT_COLS = 128;
@@ -173,59 +174,66 @@ __global__ void __launch_bounds__(threads_for(NG), 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    // Two queues served as their inputs become ready, never one blocking the
-    // other: S(next_s) needs its item's copies (first tile of an item) and a
-    // free TMEM slot; O(next_pv) needs the softmax warps' P.
+    // ---------------- S issuer ----------------
+    // S(u) = Q K^T of every M-tile in order: the first tile of an item waits
+    // for its copies, every tile for its TMEM slot (freed once the softmax
+    // warps have read out O of tile u - kSlots).  The P.V products have their
+    // own issuing thread (warp 3): one thread issuing both took 300-600 cycles
+    // per four-MMA group plus its polling and set the kernel's pace.
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(MT, NK);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(MT, HD) | (1u << 16);  // B (V) MN-major
-      int next_s = 0, next_pv = 0;
-      uint64_t t_prog = vla_globaltimer();
-      uint32_t spins = 0;
       bool ok = true;
-      while (next_pv < my_tiles) {
-        bool progressed = false;
-        if (next_s < my_tiles) {
-          const int u = next_s;
-          const int k = u / p.T, t = u % p.T, s = k % p.stages, slot = u % kSlots;
-          if ((t != 0 || mbar_test(&bb.full[s], (uint32_t)(k / p.stages) & 1u)) &&
-              mbar_test(&bb.slot_free[slot], ((uint32_t)(u / kSlots) & 1u) ^ 1u)) {
-            tc_fence_after();
-            const uint32_t st = stage0 + (uint32_t)s * p.stage_bytes;
-            const uint64_t qd = make_sw128_desc(st + (uint32_t)t * TILE_BYTES), kd = make_sw128_desc(st + q_region);
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk)
-              tc_mma_bf16(tmem + (uint32_t)slot * SLOT_COLS, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-            tc_commit(&bb.s_full[slot]);
-            ++next_s;
-            progressed = true;
-          }
+      int t = 0, s = 0, slot = 0;
+      uint32_t full_par = 0, free_par = 1;  // parities of full[s] and slot_free[slot]
+      for (int u = 0; u < my_tiles; ++u) {
+        if ((t == 0 && !mbar_wait_bounded(&bb.full[s], full_par, abort_flag)) ||
+            !mbar_wait_bounded(&bb.slot_free[slot], free_par, abort_flag)) {
+          ok = false;
+          break;
         }
-        if (next_pv < next_s) {
-          const int w = next_pv;
-          const int k = w / p.T, s = k % p.stages, slot = w % kSlots;
-          if (mbar_test(&bb.p_full[slot], (uint32_t)(w / kSlots) & 1u)) {
-            tc_fence_after();
-            const uint32_t sv = stage0 + (uint32_t)s * p.stage_bytes + q_region + NK * 128;
-            const uint32_t sc = tmem + (uint32_t)slot * SLOT_COLS;
+        tc_fence_after();
+        const uint32_t st = stage0 + (uint32_t)s * p.stage_bytes;
+        const uint64_t qd = make_sw128_desc(st + (uint32_t)t * TILE_BYTES), kd = make_sw128_desc(st + q_region);
 #pragma unroll
-            for (int kk = 0; kk < NK / 16; ++kk)
-              attn_sq::mma_ts(sc + O_OFF, sc + (uint32_t)kk * 8u, attn_sq::mn_desc(sv + (uint32_t)kk * 2048u),
-                              idesc_pv, kk > 0 ? 1u : 0u);
-            tc_commit(&bb.o_full[slot]);
-            ++next_pv;
-            progressed = true;
-          }
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc_mma_bf16(tmem + (uint32_t)slot * SLOT_COLS, qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&bb.s_full[slot]);
+        if (++slot == kSlots) slot = 0, free_par ^= 1u;
+        if (++t == p.T) {
+          t = 0;
+          if (++s == p.stages) s = 0, full_par ^= 1u;
         }
-        if (progressed) {
-          spins = 0;
-        } else if ((++spins & 255u) == 0u) {
-          if (spins == 256u) t_prog = vla_globaltimer();
-          if (*abort_flag || vla_globaltimer() - t_prog > VLA_WAIT_LIMIT_NS) {
-            ok = false;
-            break;
-          }
+      }
+      if (!ok) fail(abort_flag);
+    }
+  } else if (warp == 3) {
+    // ---------------- P.V issuer ----------------
+    // O(w) = P V of every M-tile in order, once the softmax warps have written
+    // P(w) into the slot (the item's copies have landed: its S was issued after
+    // them; the wait on full[s] only makes that explicit and passes at once).
+    if (lane == 0) {
+      constexpr uint32_t idesc_pv = make_idesc_bf16(MT, HD) | (1u << 16);  // B (V) MN-major
+      bool ok = true;
+      int t = 0, s = 0, slot = 0;
+      uint32_t full_par = 0, p_par = 0;
+      for (int w = 0; w < my_tiles; ++w) {
+        if ((t == 0 && !mbar_wait_bounded(&bb.full[s], full_par, abort_flag)) ||
+            !mbar_wait_bounded(&bb.p_full[slot], p_par, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sv = stage0 + (uint32_t)s * p.stage_bytes + q_region + NK * 128;
+        const uint32_t sc = tmem + (uint32_t)slot * SLOT_COLS;
+#pragma unroll
+        for (int kk = 0; kk < NK / 16; ++kk)
+          attn_sq::mma_ts(sc + O_OFF, sc + (uint32_t)kk * 8u, attn_sq::mn_desc(sv + (uint32_t)kk * 2048u), idesc_pv,
+                          kk > 0 ? 1u : 0u);
+        tc_commit(&bb.o_full[slot]);
+        if (++slot == kSlots) slot = 0, p_par ^= 1u;
+        if (++t == p.T) {
+          t = 0;
+          if (++s == p.stages) s = 0, full_par ^= 1u;
         }
       }
       if (!ok) fail(abort_flag);
