@@ -2,8 +2,9 @@
 (the switches are read once per process): the pipelined short attention with two
 softmax warpgroups instead of four (VLA_ATTN_PIPE_GROUPS=2) must give the same
 bits, since every query row runs the same arithmetic in either assignment of
-M-tiles to groups; the SigLIP attention with every exponential on MUFU.EX2
-(VLA_ATTN_POLY8=0) must agree with the default, which takes a quarter of them
+M-tiles to groups; the SigLIP attention with every exponential on MUFU.EX2 and
+its P.V products issued by the S issuers (VLA_ATTN_POLY8=0, VLA_ATTN_PV_WARP=0)
+must agree with the default, which takes a quarter of them
 from the FMA-pipe polynomial, within the kernels' test tolerance, and both must
 match the fp32 oracle."""
 import os
@@ -48,7 +49,8 @@ torch.save(out, sys.argv[1])
 
 
 def _child(path, **env):
-    e = dict(os.environ)
+    # the switches the parent may carry are dropped: the first child is the default
+    e = {k: v for k, v in os.environ.items() if not k.startswith("VLA_ATTN_")}
     e.update(env)
     subprocess.run([sys.executable, "-c", CHILD, str(path), ROOT], env=e, check=True, timeout=600)
     return torch.load(path)
@@ -57,7 +59,7 @@ def _child(path, **env):
 def test_attention_env_variants(cuda, tmp_path):
     from oracle import smolvla_ref as R
     base = _child(tmp_path / "default.pt")
-    alt = _child(tmp_path / "variant.pt", VLA_ATTN_PIPE_GROUPS="2", VLA_ATTN_POLY8="0")
+    alt = _child(tmp_path / "variant.pt", VLA_ATTN_PIPE_GROUPS="2", VLA_ATTN_POLY8="0", VLA_ATTN_PV_WARP="0")
     for name in ("self", "cross", "text"):
         assert torch.equal(base[name]["o"], alt[name]["o"]), f"{name}: two softmax groups changed the bits"
     s = base["siglip"]

@@ -93,8 +93,18 @@ static int attention_tc(const attn::Params& p, int batch, cudaStream_t st) {
     const int n = v != nullptr ? atoi(v) : 2;
     return n == 0 || n == 3 ? n : 2;
   }();
-  auto kern = poly8 == 0 ? attn_tc::flash_attn_tc_kernel<0>
-                         : (poly8 == 3 ? attn_tc::flash_attn_tc_kernel<3> : attn_tc::flash_attn_tc_kernel<2>);
+  // P.V products issued by warp 3 for both groups (default) or by each
+  // group's S issuer (VLA_ATTN_PV_WARP=0)
+  static const bool pv_warp = [] {
+    const char* v = getenv("VLA_ATTN_PV_WARP");
+    return !(v != nullptr && atoi(v) == 0);
+  }();
+  auto kern = pv_warp ? (poly8 == 0   ? attn_tc::flash_attn_tc_kernel<0, true>
+                         : poly8 == 3 ? attn_tc::flash_attn_tc_kernel<3, true>
+                                      : attn_tc::flash_attn_tc_kernel<2, true>)
+                      : (poly8 == 0   ? attn_tc::flash_attn_tc_kernel<0, false>
+                         : poly8 == 3 ? attn_tc::flash_attn_tc_kernel<3, false>
+                                      : attn_tc::flash_attn_tc_kernel<2, false>);
   static thread_local int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
