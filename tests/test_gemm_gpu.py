@@ -1,6 +1,8 @@
 """tcgen05 GEMM parity against a plain fp32 torch matmul of the same bf16
 operands (the reference GEMM tests compare against numpy A@B with
 atol=1e-1, rtol=1e-2: gemm/v1_test_tiled_gemm.py:147-156)."""
+import os
+
 import pytest
 import torch
 
@@ -273,4 +275,9 @@ def test_gemm_skinny(cuda, M, N, K, epi):
         outs.append(out.cpu())
     dev.sync_check()
     torch.testing.assert_close(outs[0].float(), ref, atol=3e-2, rtol=2e-2)
-    assert torch.equal(outs[0], outs[1]), "skinny and one-k-block-per-stage kernels differ"
+    if M <= 64 and K > 256 and os.environ.get("VLA_GEMM_SKINNY_DUAL", "1") != "0":
+        # two MMA-issuing threads sum the k-slab units into two fp32 accumulators
+        # that the epilogue adds: another summation order, at most one bf16 ulp
+        torch.testing.assert_close(outs[0].float(), outs[1].float(), rtol=2.0 ** -7, atol=1e-3)
+    else:
+        assert torch.equal(outs[0], outs[1]), "skinny and one-k-block-per-stage kernels differ"

@@ -203,20 +203,29 @@ static int launch_skinny(const CUtensorMap& ta, const void* A, int64_t lda, cons
   if (!rc) rc = make_tmap_bf16_kslab(&ta3, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, AR, KPS);
   if (!rc) rc = make_tmap_bf16_kslab(&tb3, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN, KPS);
   if (rc) return rc;
-  static thread_local int attr_dev_mask = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_dev_mask & (1 << (dev & 31)))) {
-    VLA_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_skinny_kernel<BN, AR, KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      Cf::SMEM_BYTES));
-    attr_dev_mask |= 1 << (dev & 31);
-  }
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int sms = device_info().num_sms;
   const int grid = (int)(tiles < sms ? tiles : sms);
+  // two MMA-issuing threads (DUAL) for 64-row copies at widths up to 128, one
+  // tile per CTA and at least two units of k-blocks; VLA_GEMM_SKINNY_DUAL=0
+  // turns it off (A/B)
+  static const bool dual_on = [] {
+    const char* v = getenv("VLA_GEMM_SKINNY_DUAL");
+    return v == nullptr || atoi(v) != 0;
+  }();
+  const int64_t units = ((K + BK - 1) / BK + KPS - 1) / KPS;
+  constexpr bool kDualShape = AR == kSkinnyRows && BN <= 128;
+  const bool dual = kDualShape && dual_on && units >= 2 && tiles <= sms;
+  auto kern = dual ? gemm_bf16_skinny_kernel<BN, AR, KPS, kDualShape> : gemm_bf16_skinny_kernel<BN, AR, KPS, false>;
+  static thread_local int attr_dev_mask[2] = {0, 0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask[dual] & (1 << (dev & 31)))) {
+    VLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES));
+    attr_dev_mask[dual] |= 1 << (dev & 31);
+  }
   prof_begin(st);
-  launch_k(gemm_bf16_skinny_kernel<BN, AR, KPS>, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep,
-           (int)M, (int)N, (int)K);
+  launch_k(kern, dim3(grid), dim3(kThreads), Cf::SMEM_BYTES, st, ta, tb, ta3, tb3, tc, tr, ep, (int)M, (int)N, (int)K);
   {
     const double out_cols = ep.act == VLA_ACT_SWIGLU ? N / 2 : N;
     double bytes = 2.0 * ((double)M * K + (double)N * K + (double)M * out_cols);

@@ -58,15 +58,36 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// Second accumulator of a DUAL launch, added to each TMEM chunk the epilogue
+// loads (the partial-sum hook of epilogue_tile).
+struct TmemPartial {
+  uint32_t base2;  // TMEM address of the second accumulator (this warp's lanes)
+  __device__ __forceinline__ void add16(int c, float* v) const {
+    float w[16];
+    tmem_ld16(base2 + (uint32_t)c, w);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += w[i];
+  }
+};
+
 // tmA / tmB: two-dimensional maps (64 x 64-row and 64 x BN boxes) for partial
 // units; tmA3 / tmB3: the k-slab maps (64, rows, K / 64) with (64, R, KPS) boxes.
-template <int BN, int AR, int KPS_ = kSkinnyKps>
+// DUAL: two threads issue the MMAs, warp 1 the even units into one
+// accumulator, lane 0 of epilogue warp 2 the odd units into a second one
+// (before it joins the epilogue), and the epilogue adds the two.  At these
+// tile sizes one thread's issue cost (~46 cycles per MMA plus the wait, fence
+// and commit of every unit) sets the main loop's pace.  The host uses it only
+// for one tile per CTA and at least two units.
+template <int BN, int AR, int KPS_ = kSkinnyKps, bool DUAL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_skinny_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmA3, const __grid_constant__ CUtensorMap tmB3,
                             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, DevEpi ep,
                             int M, int N, int K) {
   using Cf = CfgK<BN, AR, KPS_>;
+  constexpr int NACC = DUAL ? 2 : 1;  // accumulators per tile
+  constexpr int TCOLS = !DUAL ? Cf::TMEM_COLS : (4 * BN <= 128) ? 128 : (4 * BN <= 256) ? 256 : 512;
+  static_assert(!DUAL || 4 * BN <= 512, "DUAL: four BN-wide accumulators");
   constexpr int STAGES = Cf::STAGES;
   static_assert(STAGES >= 2, "unit GEMM: two stages must fit");
   constexpr int KPS = Cf::KPS;
@@ -101,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
+      mbar_init(&tfull[i], NACC);
       mbar_init(&tempty[i], 32 * kEpiWarps);
     }
     for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
@@ -114,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ep.tma_c) tma_prefetch_desc(&tmC);
     if (ep.tma_r) tma_prefetch_desc(&tmR);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Cf::TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, TCOLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -154,6 +175,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
+  // MMA issuing of accumulator h: the units u with u % NACC == h of every tile
+  auto issue = [&](int h) {
+    constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
+    int it = 0, tc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int as = tc & 1;
+      const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+      if (!mbar_wait_bounded(&tempty[as], aph ^ 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)((as * NACC + h) * BN);
+      for (int u = 0; u < nunits; ++u, ++it) {
+        if (u % NACC != h) continue;
+        const int s = it % STAGES;
+        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+        if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int cnt = unit_kbs(u);
+#pragma unroll
+        for (int i = 0; i < KPS; ++i) {
+          if (i < cnt) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(sA + s * Cf::A_UNIT + i * Cf::A_KB));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + s * Cf::B_UNIT + i * Cf::B_KB));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              tc_mma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                          ((u / NACC) | i | k) != 0 ? 1u : 0u);
+          }
+        }
+        tc_commit(&empty[s]);
+      }
+      if (!ok) break;
+      tc_commit(&tfull[as]);
+      ++tc;
+    }
+    if (!ok) {
+      if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_MMA_TIMEOUT);
+      *abort_flag = 1;
+    }
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
@@ -189,52 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, nullptr, 20000000ull);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
-      int it = 0, tc = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int as = tc & 1;
-        const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
-        if (!mbar_wait_bounded(&tempty[as], aph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(as * BN);
-        for (int u = 0; u < nunits; ++u) {
-          const int s = it % STAGES;
-          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int cnt = unit_kbs(u);
-#pragma unroll
-          for (int i = 0; i < KPS; ++i) {
-            if (i < cnt) {
-              const uint64_t adesc = make_sw128_desc(smem_u32(sA + s * Cf::A_UNIT + i * Cf::A_KB));
-              const uint64_t bdesc = make_sw128_desc(smem_u32(sB + s * Cf::B_UNIT + i * Cf::B_KB));
-#pragma unroll
-              for (int k = 0; k < BK / 16; ++k)
-                tc_mma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
-                            (u | i | k) != 0 ? 1u : 0u);
-            }
-          }
-          tc_commit(&empty[s]);
-          ++it;
-        }
-        if (!ok) break;
-        tc_commit(&tfull[as]);
-        ++tc;
-      }
-      if (!ok) {
-        if (!*abort_flag) vla_record_error(VLA_DERR_GEMM_MMA_TIMEOUT);
-        *abort_flag = 1;
-      }
-    }
+    if (lane == 0) issue(0);
   } else {
+    if (DUAL && warp == 2 && lane == 0) issue(1);
     const int q = warp & 3;
     const int part = (warp - 2) >> 2;
     EpiStore es{smem_u32(sC) + (uint32_t)((warp - 2) * 2 * kStageC), 0, 0, rbar + 2 * (warp - 2), 0u, abort_flag};
@@ -256,8 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = mb * BM + q * 32 + lane;
       es.row0 = mb * BM + q * 32;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * BN);
-      epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(as * NACC * BN);
+      if constexpr (DUAL)
+        epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane,
+                          TmemPartial{taddr + (uint32_t)BN});
+      else
+        epilogue_tile<BN>(ep, taddr, m, nb * BN, part, kEpiWarps / 4, &tmC, &tmR, es, lane);
       tc_fence_before();
       mbar_arrive(&tempty[as]);
       ++tc;
@@ -268,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cf::TMEM_COLS);
+    tmem_dealloc(tmem_base, TCOLS);
   }
 }
 
